@@ -1,0 +1,172 @@
+"""Seeded case definitions shared by ``make_golden.py`` and the tests.
+
+Everything here is deterministic from numpy ``default_rng`` seeds, so the GPU
+box regenerates the same inputs that the reference saw when the fixtures were
+made.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.gate import bf16_round
+
+# ---------------------------------------------------------------------------
+# Allocator op streams
+# ---------------------------------------------------------------------------
+
+ALLOC_STREAM_PARAMS = (
+    [dict(seed=s, L=1 + s % 3, max_blocks=64, bs=4, n_ops=60) for s in range(8)]
+    + [dict(seed=100 + s, L=2, max_blocks=256, bs=16, n_ops=80) for s in range(6)]
+    + [dict(seed=200 + s, L=1, max_blocks=12, bs=4, n_ops=60) for s in range(6)]  # exhausts
+)
+
+
+def random_op_stream(seed, L, max_blocks, bs, n_ops):
+    """A random sequence of cache API calls with reference-style seq ids."""
+    rng = np.random.default_rng(seed)
+    live: list[int] = []
+    next_id = 0
+    ops = []
+    for _ in range(n_ops):
+        r = rng.random()
+        if not live or r < 0.08:
+            ops.append(["alloc"])
+            live.append(next_id)
+            next_id += 1
+        elif r < 0.25:
+            p = int(rng.choice(live))
+            ops.append(["fork", p])
+            live.append(next_id)
+            next_id += 1
+        elif r < 0.35 and len(live) > 1:
+            s = int(rng.choice(live))
+            ops.append(["free", s])
+            live.remove(s)
+        elif r < 0.55:
+            s = int(rng.choice(live))
+            ops.append(["append", s, int(rng.integers(L)), int(rng.integers(1, 3 * bs))])
+        elif r < 0.93:
+            k = int(rng.integers(1, len(live) + 1))
+            sids = [int(x) for x in rng.choice(live, size=k, replace=False)]
+            ops.append(["append_batched", sids, int(rng.integers(L))])
+        else:
+            s = int(rng.choice(live))
+            ops.append(["trim", s, int(rng.integers(0, 4 * bs))])
+    if seed % 5 == 4:
+        ops.append(["free", next_id + 7])  # unknown seq id -> KeyError
+    return ops
+
+
+# ---------------------------------------------------------------------------
+# Attention trees
+# ---------------------------------------------------------------------------
+
+def _c(dtype, hq, hkv, d, prefix, levels, seed, pool=1024, bs=16, B=None):
+    return dict(dtype=dtype, hq=hq, hkv=hkv, d=d, prefix=prefix, levels=levels,
+                seed=seed, pool=pool, bs=bs)
+
+
+ATTN_CASES = {
+    # fp32, 8 branches x (512 shared + 64 own), pool 1024.
+    "c1": _c("f32", 16, 8, 128, 512, [(8, (64, 64))], seed=1),
+    "f32_ragged": _c("f32", 16, 8, 128, 37, [(3, (0, 40))], seed=2),
+    "bf16_b1_g1": _c("bf16", 8, 8, 128, 0, [(1, (1, 1))], seed=3),
+    "bf16_b2_g2_p15": _c("bf16", 16, 8, 128, 15, [(2, (1, 17))], seed=4),
+    "bf16_b8_g4_p16": _c("bf16", 32, 8, 128, 16, [(8, (15, 17))], seed=5),
+    "bf16_b8_g8_p17": _c("bf16", 64, 8, 128, 17, [(8, (0, 16))], seed=6),
+    "bf16_nested": _c("bf16", 32, 8, 128, 100, [(2, (5, 40)), (3, (1, 33)), (2, (0, 20))], seed=7),
+    "bf16_g4_wide": _c("bf16", 32, 8, 128, 300, [(16, (1, 64))], seed=8, pool=2048),
+    "bf16_d64": _c("bf16", 8, 4, 64, 70, [(4, (3, 30))], seed=9),
+    "f16_g2": _c("f16", 16, 8, 128, 50, [(4, (2, 20))], seed=10),
+    "bf16_64branch": _c("bf16", 32, 8, 128, 256, [(64, (16, 48))], seed=11, pool=4096),
+}
+
+
+def build_tree_ops(c):
+    """Ops that build the case's tree through the cache API.
+
+    Root gets ``prefix`` tokens; then each level forks every leaf ``fanout``
+    times, frees the parent and appends a per-child suffix with a length drawn
+    from ``[lo, hi]``.  Leaves come out in DFS order.
+    """
+    rng = np.random.default_rng(c["seed"] + 77)
+    ops = [["alloc"]]
+    next_id = 1
+    leaves = [0]
+    if c["prefix"]:
+        ops.append(["append", 0, "k_0", "v_0"])
+    for fan, (lo, hi) in c["levels"]:
+        new = []
+        for p in leaves:
+            kids = []
+            for _ in range(fan):
+                ops.append(["fork", p])
+                kids.append(next_id)
+                next_id += 1
+            ops.append(["free", p])
+            for k in kids:
+                n = int(rng.integers(lo, hi + 1))
+                if n:
+                    ops.append(["append", k, f"k_{k}", f"v_{k}", n])
+            new.extend(kids)
+        leaves = new
+    ops.append(["leaves", leaves])
+    return ops
+
+
+def attn_inputs(c):
+    """q, per-append K/V arrays (float32) and the pool permutation."""
+    rng = np.random.default_rng(c["seed"])
+    out = {"order": rng.permutation(c["pool"]).tolist()}
+    ops = build_tree_ops(c)
+    hkv, d = c["hkv"], c["d"]
+    if c["prefix"]:
+        out["k_0"] = rng.standard_normal((c["prefix"], hkv, d), dtype=np.float32)
+        out["v_0"] = rng.standard_normal((c["prefix"], hkv, d), dtype=np.float32)
+    for op in ops:
+        if op[0] == "append" and op[1] != 0:
+            n = op[4]
+            out[op[2]] = rng.standard_normal((n, hkv, d), dtype=np.float32)
+            out[op[3]] = rng.standard_normal((n, hkv, d), dtype=np.float32)
+    nleaves = len(ops[-1][1])
+    out["q"] = rng.standard_normal((nleaves, c["hq"], d), dtype=np.float32)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Gate
+# ---------------------------------------------------------------------------
+
+def _g(V, seed, scale, offset=0.0, T=0.7, penalty=1.2, K=3, hist=12, ema_old=None,
+       alpha=0.3, mult=1.25, M=10, num_active=1, step=1, window=10, initial=0.3):
+    return dict(V=V, seed=seed, scale=scale, offset=offset, T=T, penalty=penalty, K=K,
+                hist=hist, ema_old=ema_old, alpha=alpha, mult=mult, M=M,
+                num_active=num_active, step=step, window=window, initial=initial)
+
+
+GATE_CASES = (
+    [_g(151936, s, sc, ema_old=eo, num_active=na, step=st)
+     for s, sc, eo, na, st in [(0, 2.5, None, 1, 0), (1, 0.5, 11.0, 4, 3), (2, 4.0, 3.0, 7, 12),
+                               (3, 0.05, 11.9, 2, 5)]]
+    + [_g(128256, s, sc, T=1.0, K=2, M=16, ema_old=eo, num_active=na, step=st)
+       for s, sc, eo, na, st in [(10, 1.5, 4.0, 3, 20), (11, 0.02, None, 1, 0)]]
+    + [_g(V, 20 + i, sc, offset=off, hist=h, K=k, ema_old=eo, num_active=na, step=st, penalty=pen)
+       for i, (V, sc, off, h, k, eo, na, st, pen) in enumerate([
+           (1000, 0.01, 0.0, 50, 3, 6.0, 2, 2, 1.2),
+           (4096, 3.0, -2.0, 0, 3, None, 1, 0, 1.2),
+           (4096, 0.3, 1.0, 300, 5, 8.0, 5, 9, 1.2),
+           (32000, 1.0, 0.0, 40, 3, 9.0, 3, 4, 1.0),
+           (50257, 6.0, 3.0, 100, 4, 2.0, 6, 15, 1.3),
+           (257, 0.001, 0.0, 10, 3, 5.0, 1, 1, 1.2),
+           (7, 1.0, 0.0, 3, 3, None, 1, 0, 1.2),
+       ])]
+)
+
+
+def gate_inputs(c):
+    rng = np.random.default_rng(c["seed"])
+    x = bf16_round(rng.standard_normal(c["V"], dtype=np.float32) * np.float32(c["scale"])
+                   + np.float32(c["offset"]))
+    hist = [int(h) for h in rng.integers(0, c["V"], c["hist"])]
+    return x, hist

@@ -1,0 +1,186 @@
+"""Generate the golden fixtures under ``tests/golden/`` from the reference itself.
+
+Run in the build container, where the reference source tree is importable::
+
+    MENTAT_REF=<path to the reference checkout> python tests/golden/make_golden.py
+
+The GPU box does not have the reference; the tests there read only the files
+this script writes.  Inputs are regenerated from numpy ``default_rng`` seeds
+(PCG64 is stable across numpy versions), so the fixtures hold seeds, op lists
+and expected outputs, not input tensors.
+
+Reference set-up: ``adapters.attention_backend.BACKEND = "sdpa"`` (flash-attn is
+installed here but there is no GPU), the allocator's free list is replaced by
+``oracle.allocator.FifoFreeList`` (the reference's ``set.pop()`` order is a
+CPython detail), and ``torch.set_num_threads(1)`` for the gate (the CPU bf16
+``sum`` rounds per-thread partials, which makes the entropy thread-count
+dependent).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+REF = os.environ.get("MENTAT_REF", "/root/reference")
+sys.path.insert(0, REF)
+
+import adapters.attention_backend as ab  # noqa: E402
+
+ab.BACKEND = "sdpa"
+from core.paged_kv_cache import PagedKVCacheManager  # noqa: E402
+from core import generator_utils as gu  # noqa: E402
+from core.generator import MentatGenerator  # noqa: E402
+
+from oracle.allocator import FifoFreeList  # noqa: E402
+from tests.golden.cases import (  # noqa: E402
+    ALLOC_STREAM_PARAMS, ATTN_CASES, GATE_CASES, attn_inputs, build_tree_ops,
+    gate_inputs, random_op_stream,
+)
+
+
+def ref_manager(L, hkv, d, max_blocks, bs, dtype, order):
+    m = PagedKVCacheManager(L, hkv, d, max_blocks=max_blocks, block_size=bs,
+                            device="cpu", dtype=dtype)
+    m.allocator._free = FifoFreeList(order)
+    return m
+
+
+def snapshot(m) -> dict:
+    return {
+        "seqs": {str(sid): {"tables": [list(map(int, t)) for t in s.page_table],
+                            "num_tokens": list(s.num_tokens),
+                            "tail": list(s.tokens_in_last_block)}
+                 for sid, s in sorted(m._sequences.items())},
+        "refcounts": list(m.allocator.refcounts),
+        "free": m.allocator._free.as_list(),
+        "peak": m.allocator.peak_used,
+        "stats": m.get_stats(),
+    }
+
+
+def apply_op(m, op, rng_vals):
+    kind = op[0]
+    if kind == "alloc":
+        return m.allocate_sequence()
+    if kind == "fork":
+        return m.fork_sequence(op[1])
+    if kind == "free":
+        return m.free_sequence(op[1])
+    if kind == "append":
+        _, sid, layer, n = op
+        k = torch.from_numpy(rng_vals(n, m))
+        return m.append_tokens(sid, layer, k, k.clone())
+    if kind == "append_batched":
+        _, sids, layer = op
+        k = torch.from_numpy(rng_vals(len(sids), m))
+        return m.append_tokens_batched(seq_ids=sids, layer_idx=layer, k=k, v=k.clone())
+    if kind == "trim":
+        return m.trim_to_window(op[1], op[2])
+    raise ValueError(kind)
+
+
+def make_alloc_streams():
+    streams = []
+    for p in ALLOC_STREAM_PARAMS:
+        ops = random_op_stream(**p)
+        order = np.random.default_rng(p["seed"] + 1000).permutation(p["max_blocks"]).tolist()
+        m = ref_manager(p["L"], 1, 2, p["max_blocks"], p["bs"], torch.float32, order)
+        vals = lambda n, mm: np.zeros((n, 1, 2), np.float32)  # noqa: E731
+        checkpoints, error = [], None
+        for i, op in enumerate(ops):
+            try:
+                apply_op(m, op, vals)
+            except Exception as e:  # record and stop, the state after an error is not compared
+                error = {"op": i, "type": type(e).__name__, "msg": str(e)}
+                break
+            if i % 7 == 6 or i == len(ops) - 1:
+                checkpoints.append({"op": i, "snap": snapshot(m)})
+        streams.append({"params": p, "order": order, "ops": ops,
+                        "checkpoints": checkpoints, "error": error})
+    (HERE / "alloc_streams.json").write_text(json.dumps(streams))
+    print("alloc streams", len(streams))
+
+
+def make_attention():
+    out = {}
+    for name, c in ATTN_CASES.items():
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[c["dtype"]]
+        inp = attn_inputs(c)
+        order = inp["order"]
+        m = ref_manager(1, c["hkv"], c["d"], c["pool"], c["bs"], dt, order)
+        leaves = []
+        for op in build_tree_ops(c):
+            if op[0] == "append":
+                sid, arr_k, arr_v = op[1], inp[op[2]], inp[op[3]]
+                m.append_tokens(sid, 0, torch.from_numpy(arr_k).to(dt),
+                                torch.from_numpy(arr_v).to(dt))
+            elif op[0] == "alloc":
+                m.allocate_sequence()
+            elif op[0] == "fork":
+                m.fork_sequence(op[1])
+            elif op[0] == "free":
+                m.free_sequence(op[1])
+            elif op[0] == "leaves":
+                leaves = op[1]
+        q = torch.from_numpy(inp["q"]).to(dt)
+        pk, pv, cu, mx = m.build_packed_kv(leaves, 0)
+        o = ab.attn_decode(q, pk, pv, torch.arange(len(leaves) + 1, dtype=torch.int32),
+                           cu, mx, len(leaves))
+        tables = [m._sequences[s].page_table[0] for s in leaves]
+        out[f"{name}__out"] = o.float().numpy()
+        out[f"{name}__tables"] = np.array([t + [-1] * (max(map(len, tables)) - len(t)) for t in tables], np.int32) if tables and max(map(len, tables)) else np.zeros((len(leaves), 0), np.int32)
+        out[f"{name}__lens"] = np.array([m.get_kv_length(s) for s in leaves], np.int32)
+        out[f"{name}__cu"] = cu.numpy()
+        out[f"{name}__maxlen"] = np.array(mx)
+        out[f"{name}__refcounts"] = np.array(m.allocator.refcounts, np.int32)
+    np.savez_compressed(HERE / "attention.npz", **out)
+    print("attention cases", len(ATTN_CASES))
+
+
+def make_gate():
+    torch.set_num_threads(1)
+    gen_self = SimpleNamespace(soft_explore_window=None, soft_explore_initial=None)
+    res = []
+    for c in GATE_CASES:
+        x32, hist = gate_inputs(c)
+        x = torch.from_numpy(x32).to(torch.bfloat16)
+        assert np.array_equal(x.float().numpy(), x32), "inputs must be bf16 values"
+        H = gu.compute_entropy(x, c["T"])
+        pen = gu.apply_repetition_penalty(x, hist, penalty=c["penalty"])
+        lp = F.log_softmax(pen, dim=-1)
+        am = int(torch.argmax(lp).item())
+        tv, ti = torch.topk(lp, c["K"])
+        gen_self.soft_explore_window = c["window"]
+        gen_self.soft_explore_initial = c["initial"]
+        ema_old = c["ema_old"]
+        ema = H if ema_old is None else (c["alpha"] * H) + ((1.0 - c["alpha"]) * ema_old)
+        dyn = gu.adaptive_threshold(c["mult"], c["M"], c["num_active"])
+        warm = MentatGenerator._soft_explore_factor(gen_self, c["step"])
+        tau = ema * dyn * warm
+        branch = (H > tau) and ((c["M"] - c["num_active"]) >= c["K"])
+        res.append({
+            "case": c, "entropy": H, "ema": ema, "tau": tau, "branch": bool(branch),
+            "argmax": am, "argmax_lp": float(lp[am].item()),
+            "topk_ids": ti.tolist(), "topk_lps": tv.float().tolist(),
+            "pen_entropy": gu.compute_entropy(pen),
+            "lp_sha": int(np.frombuffer(lp.view(torch.int16).numpy().tobytes(), np.uint8).astype(np.uint64).sum()),
+        })
+    (HERE / "gate.json").write_text(json.dumps(res))
+    print("gate cases", len(res))
+
+
+if __name__ == "__main__":
+    make_alloc_streams()
+    make_attention()
+    make_gate()

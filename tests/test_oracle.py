@@ -1,0 +1,137 @@
+"""The oracle against the reference's own outputs (golden fixtures)."""
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle.allocator import OraclePagedKV
+from oracle.attention import paged_decode, unique_kv_bytes
+from oracle.gate import gate_leaf, log_softmax_bf16, apply_penalty, bf16_round
+from tests.golden.cases import ATTN_CASES, attn_inputs, build_tree_ops, gate_inputs
+
+HERE = os.path.dirname(__file__)
+
+
+def _streams():
+    with open(os.path.join(HERE, "golden", "alloc_streams.json")) as f:
+        return json.load(f)
+
+
+def apply_op(m, op):
+    kind = op[0]
+    if kind == "alloc":
+        return m.allocate_sequence()
+    if kind == "fork":
+        return m.fork_sequence(op[1])
+    if kind == "free":
+        return m.free_sequence(op[1])
+    if kind == "append":
+        _, sid, layer, n = op
+        z = np.zeros((n, 1, 2), np.float32)
+        return m.append_tokens(sid, layer, z, z)
+    if kind == "append_batched":
+        _, sids, layer = op
+        z = np.zeros((len(sids), 1, 2), np.float32)
+        return m.append_tokens_batched(sids, layer, z, z)
+    if kind == "trim":
+        return m.trim_to_window(op[1], op[2])
+    raise ValueError(kind)
+
+
+def snap(m):
+    s = m.snapshot()
+    s["seqs"] = {str(k): v for k, v in s["seqs"].items()}
+    s["stats"] = m.get_stats()
+    return s
+
+
+@pytest.mark.parametrize("idx", range(20))
+def test_oracle_alloc_stream(idx):
+    st = _streams()[idx]
+    p = st["params"]
+    m = OraclePagedKV(p["L"], 1, 2, p["max_blocks"], p["bs"], order=st["order"], with_data=False)
+    cps = {c["op"]: c["snap"] for c in st["checkpoints"]}
+    err = st["error"]
+    for i, op in enumerate(st["ops"]):
+        if err and i == err["op"]:
+            exc = {"RuntimeError": RuntimeError, "KeyError": KeyError,
+                   "AssertionError": AssertionError}[err["type"]]
+            with pytest.raises(exc) as ei:
+                apply_op(m, op)
+            assert str(ei.value) == err["msg"]
+            return
+        apply_op(m, op)
+        if i in cps:
+            assert snap(m) == cps[i], f"op {i}"
+    assert err is None
+
+
+@pytest.mark.parametrize("name", sorted(ATTN_CASES))
+def test_oracle_attention(name):
+    c = ATTN_CASES[name]
+    g = np.load(os.path.join(HERE, "golden", "attention.npz"))
+    inp = attn_inputs(c)
+    dt = {"f32": np.float32, "bf16": np.float32, "f16": np.float16}[c["dtype"]]
+    rnd = (lambda a: bf16_round(a)) if c["dtype"] == "bf16" else (lambda a: a.astype(dt).astype(np.float32))
+    m = OraclePagedKV(1, c["hkv"], c["d"], c["pool"], c["bs"], order=inp["order"])
+    leaves = []
+    for op in build_tree_ops(c):
+        if op[0] == "append":
+            m.append_tokens(op[1], 0, rnd(inp[op[2]]), rnd(inp[op[3]]))
+        elif op[0] == "alloc":
+            m.allocate_sequence()
+        elif op[0] == "fork":
+            m.fork_sequence(op[1])
+        elif op[0] == "free":
+            m.free_sequence(op[1])
+        else:
+            leaves = op[1]
+    tables = [m._sequences[s].page_table[0] for s in leaves]
+    lens = [m.get_kv_length(s) for s in leaves]
+    gt = g[f"{name}__tables"]
+    for i, t in enumerate(tables):
+        assert list(gt[i][: len(t)]) == t
+    assert lens == g[f"{name}__lens"].tolist()
+    assert m.allocator.refcounts == g[f"{name}__refcounts"].tolist()
+    o = paged_decode(rnd(inp["q"]), m.k_pools[0], m.v_pools[0], tables, lens, c["bs"])
+    ref = g[f"{name}__out"]
+    if c["dtype"] == "f32":
+        np.testing.assert_allclose(o, ref, atol=1e-5, rtol=0)
+    else:
+        np.testing.assert_allclose(o, ref, atol=2e-3, rtol=1e-2)
+
+
+def test_c1_unique_bytes():
+    c = ATTN_CASES["c1"]
+    g = np.load(os.path.join(HERE, "golden", "attention.npz"))
+    tabs = [t[t >= 0] for t in g["c1__tables"]]
+    assert unique_kv_bytes(tabs, g["c1__lens"], 16, 8, 128, 4) == 8388608
+    assert c["prefix"] == 512
+
+
+def test_oracle_gate():
+    with open(os.path.join(HERE, "golden", "gate.json")) as f:
+        gold = json.load(f)
+    for g in gold:
+        c = g["case"]
+        x, hist = gate_inputs(c)
+        r = gate_leaf(x, hist, temperature=c["T"], penalty=c["penalty"], K=c["K"],
+                      ema_old=c["ema_old"], alpha=c["alpha"], mult=c["mult"], M=c["M"],
+                      num_active=c["num_active"], step=c["step"], window=c["window"],
+                      initial=c["initial"])
+        assert r["entropy"] == g["entropy"], c
+        assert r["ema"] == g["ema"] and r["tau"] == g["tau"] and r["branch"] == g["branch"]
+        assert r["argmax"] == g["argmax"] and r["argmax_lp"] == g["argmax_lp"]
+        assert r["pen_entropy"] == g["pen_entropy"], c
+        # top-k: identical values; indices identical except inside tie groups
+        assert r["topk_lps"] == g["topk_lps"]
+        lp = log_softmax_bf16(apply_penalty(x, hist, c["penalty"]))
+        import torch
+        lpt = torch.from_numpy(lp).to(torch.bfloat16)
+        sha = int(np.frombuffer(lpt.view(torch.int16).numpy().tobytes(), np.uint8).astype(np.uint64).sum())
+        assert sha == g["lp_sha"]
+        for i, v in zip(g["topk_ids"], g["topk_lps"]):
+            assert lp[i] == v
+        assert sorted(r["topk_ids"]) == sorted(g["topk_ids"]) or len(set(g["topk_lps"])) < len(g["topk_lps"]) or np.sum(lp == g["topk_lps"][-1]) > 1
