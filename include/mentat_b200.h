@@ -1,0 +1,203 @@
+/*
+ * mentat_b200.h -- C ABI of libmentat_b200.so, the B200 (sm_100a) implementation of
+ * MENTAT's entropy-gated prefix-tree decode path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t, is
+ * stream-ordered, never allocates, and returns an int status (MENTAT_OK == 0,
+ * negative on argument or launch errors).  Errors that can only be known on
+ * the device (out of blocks, refcount underflow, plan overflow) are written to
+ * the cache's control words (ctrl[MENTAT_CTRL_ERROR], ctrl[MENTAT_CTRL_ERRARG])
+ * and read by the host at its next synchronisation point.
+ *
+ * Reference interfaces each entry point replaces are cited as
+ * <file>:<line> of SkyeGunasekaran/MENTAT.
+ */
+#ifndef MENTAT_B200_H
+#define MENTAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MENTAT_ABI_VERSION 1
+
+/* status codes (returned) and device error codes (ctrl[MENTAT_CTRL_ERROR]) */
+#define MENTAT_OK 0
+#define MENTAT_ERR_ARG (-1)          /* invalid argument */
+#define MENTAT_ERR_CUDA (-2)         /* a launch failed */
+#define MENTAT_ERR_UNSUPPORTED (-3)  /* shape / dtype not built */
+#define MENTAT_DEV_OUT_OF_BLOCKS 1   /* paged_kv_cache.py:46-50 RuntimeError */
+#define MENTAT_DEV_REF_FREE 2        /* paged_kv_cache.py:59 AssertionError */
+#define MENTAT_DEV_RELEASE_FREE 3    /* paged_kv_cache.py:63 AssertionError */
+#define MENTAT_DEV_PLAN_OVERFLOW 4   /* decode plan exceeded its workspace */
+#define MENTAT_DEV_TABLE_OVERFLOW 5  /* a sequence outgrew max_blocks_per_seq */
+
+/* dtypes */
+#define MENTAT_F32 0
+#define MENTAT_BF16 1
+#define MENTAT_F16 2
+
+/* control words of the block allocator, int64 each */
+#define MENTAT_CTRL_HEAD 0    /* free-ring pops so far (monotonic) */
+#define MENTAT_CTRL_TAIL 1    /* free-ring pushes so far (monotonic); free = tail - head */
+#define MENTAT_CTRL_PEAK 2    /* high-water mark of blocks in use (paged_kv_cache.py:41-43) */
+#define MENTAT_CTRL_ERROR 3   /* first device error code, 0 if none */
+#define MENTAT_CTRL_ERRARG 4  /* its argument (block id, slot) */
+#define MENTAT_CTRL_ALLOCS 5  /* blocks allocated so far */
+#define MENTAT_CTRL_COWS 6    /* copy-on-write block copies so far */
+#define MENTAT_CTRL_WORDS 16
+
+/*
+ * Paged KV cache state, all device memory owned by the caller.
+ * Replaces PagedKVCacheManager's pools, BlockAllocator and SequenceState
+ * (core/paged_kv_cache.py:21-140).  Sequences live in slots [0, max_seqs).
+ */
+typedef struct mentat_kv_cache {
+    int32_t num_layers;
+    int32_t num_blocks;          /* max_blocks of the reference */
+    int32_t block_size;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t dtype;               /* MENTAT_F32 / MENTAT_BF16 / MENTAT_F16 */
+    int32_t max_seqs;
+    int32_t max_blocks_per_seq;
+    void* k_pool;                /* [num_layers][num_blocks][block_size][num_kv_heads][head_dim] */
+    void* v_pool;                /* same */
+    int32_t* refcounts;          /* [num_blocks] */
+    int32_t* free_ring;          /* [num_blocks], FIFO of free block ids */
+    int64_t* ctrl;               /* [MENTAT_CTRL_WORDS] */
+    int32_t* tables;             /* [num_layers][max_seqs][max_blocks_per_seq] */
+    int32_t* nblocks;            /* [num_layers][max_seqs] table lengths */
+    int32_t* ntok;               /* [num_layers][max_seqs] num_tokens */
+    int32_t* tail;               /* [num_layers][max_seqs] tokens_in_last_block */
+    int32_t* scratch;            /* [mentat_kv_scratch_ints(max_seqs)] */
+} mentat_kv_cache;
+
+int mentat_abi_version(void);
+const char* mentat_status_string(int status);
+int64_t mentat_kv_scratch_ints(int32_t max_seqs);
+
+/* BlockAllocator.__init__ (paged_kv_cache.py:26-30): refcounts 0, every block
+ * free, in the order given by initial_order (device int32[num_blocks]; NULL
+ * means 0..num_blocks-1), which is also the pop order. */
+int mentat_kv_init(const mentat_kv_cache* c, const int32_t* initial_order, cudaStream_t s);
+
+/* allocate_sequence (paged_kv_cache.py:143-150): empty tables in every layer. */
+int mentat_kv_seq_reset(const mentat_kv_cache* c, int32_t slot, cudaStream_t s);
+
+/* fork_sequence (paged_kv_cache.py:152-170): copy every layer's table and
+ * counters of parent_slot to child_slot and ref() every block.
+ * max_nblocks is the parent's longest table (a launch-size hint). */
+int mentat_kv_fork(const mentat_kv_cache* c, int32_t parent_slot, int32_t child_slot,
+                   int32_t max_nblocks, cudaStream_t s);
+
+/* free_sequence (paged_kv_cache.py:172-176): release() every block, layer by
+ * layer in table order; blocks reaching refcount 0 join the free FIFO in that
+ * order. */
+int mentat_kv_free(const mentat_kv_cache* c, int32_t slot, int32_t max_nblocks, cudaStream_t s);
+
+/* append_tokens_batched (paged_kv_cache.py:227-284): one token for each of n
+ * sequences (slots, device int32[n]) in layer `layer`: new block when the tail
+ * is full or the table empty, copy-on-write of a shared tail, then the scatter
+ * of k/v rows ([n][num_kv_heads][head_dim], token stride k_stride/v_stride in
+ * elements).  n <= 1024 per call. */
+int mentat_kv_append_batched(const mentat_kv_cache* c, int32_t layer, const int32_t* slots,
+                             int32_t n, const void* k, int64_t k_stride, const void* v,
+                             int64_t v_stride, cudaStream_t s);
+
+/* append_tokens (paged_kv_cache.py:178-225): n tokens for one sequence. */
+int mentat_kv_append(const mentat_kv_cache* c, int32_t layer, int32_t slot, int32_t n,
+                     const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                     cudaStream_t s);
+
+/* trim_to_window (paged_kv_cache.py:370-417), every layer of one sequence. */
+int mentat_kv_trim(const mentat_kv_cache* c, int32_t slot, int32_t window, cudaStream_t s);
+
+/* build_packed_kv's gather (paged_kv_cache.py:347-359): materialise the packed
+ * (sum_len, num_kv_heads, head_dim) K and V of n sequences; cu_seqlens is the
+ * device int32[n+1] prefix sum of their lengths. */
+int mentat_kv_gather(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
+                     const int32_t* cu_seqlens, int64_t total_tokens, void* out_k, void* out_v,
+                     cudaStream_t s);
+
+/*
+ * Tree-aware paged GQA decode attention.  Replaces build_packed_kv + attn_decode
+ * (paged_kv_cache.py:289-368, attention_backend.py:192-228 -> flash_attn varlen
+ * or _sdpa_decode :99-168).  Sequences are the slots of the batch, in batch
+ * order; KV blocks shared by adjacent sequences of the batch (found from the
+ * block tables) are read once for all of them.  n <= 512 per call.
+ *
+ * q:   [n][num_q_heads][head_dim], token stride q_stride (elements), cache dtype.
+ * out: same layout, out_stride.
+ * scale: softmax scale (the reference uses 1/sqrt(head_dim)).
+ * workspace: device memory of mentat_decode_workspace_bytes(...) bytes.
+ */
+int64_t mentat_decode_workspace_bytes(int32_t n, int32_t num_q_heads, int32_t head_dim,
+                                      int32_t max_parts);
+int32_t mentat_decode_max_parts(int32_t n, int32_t max_len, int32_t block_size);
+int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
+                        const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
+                        int64_t out_stride, float scale, void* workspace, int64_t workspace_bytes,
+                        int32_t max_parts, cudaStream_t s);
+
+/* Stage timing of mentat_paged_decode (plan, units, merge) with CUDA events
+ * recorded on the launch stream, for up to max_records launches (0 disables).
+ * No counterpart in the reference; used by the benchmark's roofline report.
+ * collect waits for the last recorded launch, returns the summed milliseconds
+ * of each stage and the number of launches, and restarts the record. */
+int mentat_profile_enable(int32_t max_records);
+int mentat_profile_collect(double* stage_ms, int32_t* launches);
+
+/*
+ * Fused entropy gate over the full vocabulary, one leaf per row.  Replaces
+ * compute_entropy (generator_utils.py:196-202), apply_repetition_penalty
+ * (:205-230), adaptive_threshold (:247-253), and the arithmetic of
+ * MentatGenerator._step_leaf / _do_branch / _do_extend / _soft_explore_factor
+ * (generator.py:275-374).
+ */
+#define MENTAT_GATE_MAXK 8
+typedef struct mentat_gate_params {
+    double temperature;     /* entropy temperature (generator.py:342) */
+    double penalty;         /* repetition penalty (generator.py:363-366) */
+    double alpha;           /* entropy EMA alpha (generator.py:349) */
+    double mult;            /* relative_entropy_multiplier (generator.py:352) */
+    double initial;         /* soft_explore_initial (generator.py:331) */
+    int32_t K;              /* branching factor, <= MENTAT_GATE_MAXK */
+    int32_t M;              /* max_active_branches */
+    int32_t num_active;     /* active leaves at the start of the step */
+    int32_t step;           /* decode step */
+    int32_t window;         /* soft_explore_window */
+    int32_t pad;
+} mentat_gate_params;
+
+typedef struct mentat_gate_out {
+    double entropy;         /* compute_entropy(logits, T), reduced-precision rounding chain */
+    double entropy_acc;     /* float-accurate entropy of softmax(logits / T) */
+    double pen_entropy;     /* compute_entropy(penalised) at T = 1 (generator.py:293) */
+    double ema;             /* updated entropy EMA */
+    double tau;             /* branch threshold */
+    int32_t branch;         /* 1 = branch (top-K), 0 = extend (argmax) */
+    int32_t argmax;
+    float argmax_lp;
+    int32_t topk_ids[MENTAT_GATE_MAXK];
+    float topk_lps[MENTAT_GATE_MAXK];
+    int32_t pad[3];
+} mentat_gate_out;
+
+/* logits: [n][vocab] (row stride in elements), dtype of the model.
+ * hist_ptr/hist_ids: CSR of each leaf's generated token ids (duplicates allowed).
+ * ema_old: device double[n]; NaN means "no EMA yet" (TreeNode.entropy_ema None).
+ * out: device mentat_gate_out[n]. */
+int mentat_gate_step(const void* logits, int32_t dtype, int32_t n, int32_t vocab,
+                     int64_t row_stride, const int32_t* hist_ptr, const int32_t* hist_ids,
+                     const double* ema_old, const mentat_gate_params* params,
+                     mentat_gate_out* out, cudaStream_t s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MENTAT_B200_H */

@@ -1,0 +1,110 @@
+// Shared device helpers of libmentat_b200 (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mentat_b200.h"
+
+#define MENTAT_CHECK_LAUNCH()                          \
+    do {                                               \
+        if (cudaPeekAtLastError() != cudaSuccess) {    \
+            (void)cudaGetLastError();                  \
+            return MENTAT_ERR_CUDA;                    \
+        }                                              \
+    } while (0)
+
+namespace mentat {
+
+// ---------------------------------------------------------------------------
+// element types
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static constexpr int code = MENTAT_F32;
+    __device__ __forceinline__ static float to_f(float x) { return x; }
+    __device__ __forceinline__ static float from_f(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static constexpr int code = MENTAT_BF16;
+    __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+template <> struct Elem<__half> {
+    static constexpr int code = MENTAT_F16;
+    __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+    __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+};
+
+__host__ __device__ inline int dtype_bytes(int dtype) { return dtype == MENTAT_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------------------
+// cache indexing
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t seq_index(const mentat_kv_cache& c, int layer, int slot) {
+    return (int64_t)layer * c.max_seqs + slot;
+}
+__device__ __forceinline__ int32_t* table_row(const mentat_kv_cache& c, int layer, int slot) {
+    return c.tables + ((int64_t)layer * c.max_seqs + slot) * c.max_blocks_per_seq;
+}
+// element offset of the (layer, block, slot-in-block) row; a row is Hkv*D elements
+__device__ __forceinline__ int64_t pool_row(const mentat_kv_cache& c, int layer, int block, int s) {
+    return (((int64_t)layer * c.num_blocks + block) * c.block_size + s) * (int64_t)c.num_kv_heads *
+           c.head_dim;
+}
+
+// first device error wins; later ones are dropped
+__device__ __forceinline__ void set_error(const mentat_kv_cache& c, int code, int64_t arg) {
+    unsigned long long* e = reinterpret_cast<unsigned long long*>(c.ctrl + MENTAT_CTRL_ERROR);
+    if (atomicCAS(e, 0ull, (unsigned long long)code) == 0ull) c.ctrl[MENTAT_CTRL_ERRARG] = arg;
+}
+__device__ __forceinline__ bool has_error(const mentat_kv_cache& c) {
+    return *((volatile int64_t*)(c.ctrl + MENTAT_CTRL_ERROR)) != 0;
+}
+
+// ---------------------------------------------------------------------------
+// block-wide exclusive scan of ints (blockDim.x a multiple of 32, <= 1024)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* smem32) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) smem32[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nwarps ? smem32[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        smem32[lane] = w;
+    }
+    __syncthreads();
+    int base = warp ? smem32[warp - 1] : 0;
+    *total = smem32[nwarps - 1];
+    __syncthreads();
+    return base + x - v;
+}
+
+// copy `n` bytes with a whole block; 16-byte vectors when everything is aligned
+__device__ __forceinline__ void block_copy_bytes(void* dst, const void* src, int64_t n) {
+    if ((((uintptr_t)dst | (uintptr_t)src | (uintptr_t)n) & 15) == 0) {
+        const uint4* s = reinterpret_cast<const uint4*>(src);
+        uint4* d = reinterpret_cast<uint4*>(dst);
+        for (int64_t i = threadIdx.x; i < n / 16; i += blockDim.x) d[i] = s[i];
+        return;
+    }
+    const uint8_t* s = reinterpret_cast<const uint8_t*>(src);
+    uint8_t* d = reinterpret_cast<uint8_t*>(dst);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) d[i] = s[i];
+}
+
+}  // namespace mentat

@@ -1,0 +1,494 @@
+// Tree-aware paged GQA decode attention (replaces build_packed_kv + attn_decode
+// of the reference: core/paged_kv_cache.py:289-368, adapters/attention_backend.py:192-228).
+//
+// Three stream-ordered launches:
+//   1. k_plan    (1 CTA)  - reads the batch's block tables, finds the token
+//      prefixes that adjacent sequences share (longest common block prefix),
+//      builds the LCP-interval tree of the batch and cuts every node of it
+//      (a token range shared by a contiguous run of sequences) into units of
+//      <= CHUNK tokens x <= 16 query rows.  Each unit gets a partial-result
+//      ordinal that is unique along every sequence's root-to-leaf path.
+//   2. k_units   (persistent CTAs, dynamic unit queue) - one unit x one kv
+//      head per work item: stream the unit's K/V tiles once, compute scores
+//      for all its query rows (GQA group x sharing sequences), online
+//      softmax in base 2, and write the unnormalised partial (m, l, o).
+//   3. k_merge   - log-sum-exp merge of each (sequence, q head)'s partials.
+// A shared prefix is therefore read once per unit instead of once per branch,
+// and the packed KV of the reference is never materialised.
+
+#include "common.cuh"
+
+namespace mentat {
+
+constexpr int PLAN_HDR = 64;        // ints: [0] units, [1] work counter, [2] error
+constexpr int UNIT_INTS = 8;        // seq_lo, seq_hi, tok0, tok1, ordinal
+constexpr int CHUNK = 256;          // tokens per unit
+constexpr int MAX_ROWS = 16;        // query rows per unit on the FFMA path
+constexpr int PLAN_MAX_SEQS = 512;  // sequences per launch (callers split larger batches)
+
+struct DecodeWs {
+    int32_t* hdr;
+    int32_t* nparts;  // [n]
+    int32_t* units;   // [n * max_parts][UNIT_INTS]
+    float* part_ml;   // [n][max_parts][Hq][2]
+    float* part_o;    // [n][max_parts][Hq][D]
+};
+
+__host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline void ws_carve(void* base, int n, int hq, int d, int max_parts, DecodeWs* w,
+                                         int64_t* total) {
+    int64_t off = 0;
+    char* b = reinterpret_cast<char*>(base);
+    auto take = [&](int64_t bytes) {
+        char* p = b ? b + off : nullptr;
+        off = align_up(off + bytes, 256);
+        return p;
+    };
+    w->hdr = reinterpret_cast<int32_t*>(take(PLAN_HDR * 4));
+    w->nparts = reinterpret_cast<int32_t*>(take((int64_t)n * 4));
+    w->units = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
+    w->part_ml = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * 2 * 4));
+    w->part_o = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * d * 4));
+    *total = off;
+}
+
+// ---------------------------------------------------------------------------
+// 1. plan
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeWs ws, int max_parts) {
+    __shared__ int s_len[PLAN_MAX_SEQS];
+    __shared__ int s_slot[PLAN_MAX_SEQS];
+    __shared__ int s_h[PLAN_MAX_SEQS + 1];    // h[i] = LCP(i-1, i) in tokens, h[0] = h[n] = 0
+    __shared__ int s_top[PLAN_MAX_SEQS + 1];  // deepest node covering i-1, i after boundary i
+    __shared__ int s_nlo[PLAN_MAX_SEQS], s_nhi[PLAN_MAX_SEQS], s_ndep[PLAN_MAX_SEQS], s_npar[PLAN_MAX_SEQS];
+    __shared__ int s_post[PLAN_MAX_SEQS];     // node ids in pop (post) order
+    __shared__ int s_nbase[PLAN_MAX_SEQS], s_nchunk[PLAN_MAX_SEQS];
+    __shared__ int s_seg_units[2 * PLAN_MAX_SEQS];  // internal nodes, then leaves
+    __shared__ int s_seg_first[2 * PLAN_MAX_SEQS];
+    __shared__ int smem32[32];
+    __shared__ int s_nnodes, s_err;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bs = c.block_size;
+
+    for (int i = tid; i < n; i += blockDim.x) {
+        int slot = slots[i];
+        if (slot < 0 || slot >= c.max_seqs) slot = 0;
+        s_slot[i] = slot;
+        s_len[i] = c.ntok[seq_index(c, layer, slot)];
+    }
+    if (tid == 0) {
+        s_h[0] = 0;
+        s_h[n] = 0;
+        s_err = 0;
+    }
+    __syncthreads();
+
+    // LCP of adjacent sequences, in tokens (one warp per pair)
+    for (int i = 1 + warp; i < n; i += blockDim.x / 32) {
+        const int la = s_len[i - 1], lb = s_len[i];
+        const int m = min((la + bs - 1) / bs, (lb + bs - 1) / bs);
+        const int32_t* ta = table_row(c, layer, s_slot[i - 1]);
+        const int32_t* tb = table_row(c, layer, s_slot[i]);
+        int first = m;
+        if (s_slot[i - 1] != s_slot[i]) {
+            for (int j0 = 0; j0 < m; j0 += 32 * 8) {
+                int mis = m;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    int j = j0 + u * 32 + lane;
+                    if (j < m && ta[j] != tb[j]) mis = min(mis, j);
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mis = min(mis, __shfl_xor_sync(0xffffffffu, mis, o));
+                if (mis < m) {
+                    first = mis;
+                    break;
+                }
+            }
+        }
+        if (lane == 0) s_h[i] = min(min(first * bs, la), lb);
+    }
+    __syncthreads();
+
+    // LCP-interval tree (one thread, O(n))
+    if (tid == 0) {
+        int sp = 0;           // stack of node ids; the virtual root (-1) has depth 0
+        int* stk = s_nbase;   // stack storage until the bases are computed
+        int nn = 0, npost = 0;
+        s_top[0] = -1;
+        for (int i = 1; i <= n; ++i) {
+            const int h = (i < n) ? s_h[i] : 0;
+            int lo = i - 1;
+            while (sp > 0 && s_ndep[stk[sp - 1]] > h) {
+                const int x = stk[--sp];
+                s_nhi[x] = i - 1;
+                s_post[npost++] = x;
+                lo = s_nlo[x];
+                const int topdep = sp > 0 ? s_ndep[stk[sp - 1]] : 0;
+                if (topdep >= h) s_npar[x] = sp > 0 ? stk[sp - 1] : -1;
+                else s_npar[x] = nn;  // the node about to be pushed with depth h
+            }
+            const int topdep = sp > 0 ? s_ndep[stk[sp - 1]] : 0;
+            if (topdep < h) {
+                s_nlo[nn] = lo;
+                s_ndep[nn] = h;
+                s_npar[nn] = -2;
+                stk[sp++] = nn++;
+            }
+            s_top[i] = sp > 0 ? stk[sp - 1] : -1;
+        }
+        s_nnodes = nn;
+        // partial ordinals: parents before children (reverse post order)
+        for (int k = npost - 1; k >= 0; --k) {
+            const int x = s_post[k];
+            const int p = s_npar[x];
+            const int pdep = p >= 0 ? s_ndep[p] : 0;
+            s_nchunk[x] = (s_ndep[x] - pdep + CHUNK - 1) / CHUNK;
+            s_nbase[x] = p >= 0 ? s_nbase[p] + s_nchunk[p] : 0;
+        }
+    }
+    __syncthreads();
+    const int nn = s_nnodes;
+    const int spu = max(1, MAX_ROWS / G);  // sequences per unit
+    for (int s = tid; s < nn + n; s += blockDim.x) {
+        int cnt;
+        if (s < nn) {
+            const int width = s_nhi[s] - s_nlo[s] + 1;
+            cnt = s_nchunk[s] * ((width + spu - 1) / spu);
+        } else {
+            const int i = s - nn;
+            const int a = s_top[i], b = s_top[i + 1];
+            const int da = a >= 0 ? s_ndep[a] : 0, db = b >= 0 ? s_ndep[b] : 0;
+            const int node = da >= db ? a : b;
+            const int d0 = node >= 0 ? s_ndep[node] : 0;
+            const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
+            const int ch = (s_len[i] - d0 + CHUNK - 1) / CHUNK;
+            cnt = ch;
+            ws.nparts[i] = base + ch;
+            if (base + ch > max_parts) atomicExch(&s_err, 1);
+        }
+        s_seg_units[s] = cnt;
+    }
+    __syncthreads();
+    {
+        const int s0 = 2 * tid, s1 = 2 * tid + 1;
+        const int c0 = s0 < nn + n ? s_seg_units[s0] : 0;
+        const int c1 = s1 < nn + n ? s_seg_units[s1] : 0;
+        int total;
+        const int e = block_exclusive_scan(c0 + c1, &total, smem32);
+        if (s0 < nn + n) s_seg_first[s0] = e;
+        if (s1 < nn + n) s_seg_first[s1] = e + c0;
+        if (tid == 0) {
+            if ((int64_t)total > (int64_t)n * max_parts) s_err = 1;
+            ws.hdr[0] = s_err ? 0 : total;
+            ws.hdr[1] = 0;
+            ws.hdr[2] = s_err;
+            if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, total);
+        }
+        __syncthreads();
+        if (s_err) return;
+        for (int u = tid; u < total; u += blockDim.x) {
+            int lo = 0, hi = nn + n - 1;  // last segment whose first unit <= u
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_seg_first[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            const int s = lo, k = u - s_seg_first[s];
+            int q_lo, q_hi, t0, t1, ord;
+            if (s < nn) {
+                const int width = s_nhi[s] - s_nlo[s] + 1;
+                const int ngroups = (width + spu - 1) / spu;
+                const int ch = k / ngroups, rg = k % ngroups;
+                const int p = s_npar[s];
+                const int pdep = p >= 0 ? s_ndep[p] : 0;
+                q_lo = s_nlo[s] + rg * spu;
+                q_hi = min(s_nhi[s], q_lo + spu - 1);
+                t0 = pdep + ch * CHUNK;
+                t1 = min(s_ndep[s], t0 + CHUNK);
+                ord = s_nbase[s] + ch;
+            } else {
+                const int i = s - nn;
+                const int a = s_top[i], b = s_top[i + 1];
+                const int da = a >= 0 ? s_ndep[a] : 0, db = b >= 0 ? s_ndep[b] : 0;
+                const int node = da >= db ? a : b;
+                const int d0 = node >= 0 ? s_ndep[node] : 0;
+                const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
+                q_lo = q_hi = i;
+                t0 = d0 + k * CHUNK;
+                t1 = min(s_len[i], t0 + CHUNK);
+                ord = base + k;
+            }
+            int32_t* U = ws.units + (int64_t)u * UNIT_INTS;
+            U[0] = q_lo; U[1] = q_hi; U[2] = t0; U[3] = t1; U[4] = ord;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. units (FFMA path: any dtype, <= 16 query rows per unit)
+// ---------------------------------------------------------------------------
+constexpr int TT = 32;  // tokens per tile
+constexpr int UNIT_THREADS = 128;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(UNIT_THREADS)
+k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict__ q, int64_t q_stride, int Hq,
+        float qscale, DecodeWs ws, int max_parts) {
+    constexpr int TS = UNIT_THREADS / D;  // token splits in the PV stage
+    constexpr int KP = D + 1;             // padded K row (conflict-free column reads)
+    __shared__ float q_s[MAX_ROWS][D];
+    __shared__ float k_s[TT][KP];
+    __shared__ float v_s[TT][D];
+    __shared__ float p_s[MAX_ROWS][TT];
+    __shared__ float m_s[MAX_ROWS], l_s[MAX_ROWS], a_s[MAX_ROWS];
+    __shared__ float red_s[TS > 1 ? TS : 1][TS > 1 ? MAX_ROWS : 1][TS > 1 ? D : 1];
+    __shared__ int s_work;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int Hkv = c.num_kv_heads, G = Hq / Hkv, bs = c.block_size;
+    const int nunits = ws.hdr[0];
+    const int64_t nwork = (int64_t)nunits * Hkv;
+    const T* kpool = reinterpret_cast<const T*>(c.k_pool);
+    const T* vpool = reinterpret_cast<const T*>(c.v_pool);
+    for (;;) {
+        if (tid == 0) s_work = atomicAdd(&ws.hdr[1], 1);
+        __syncthreads();
+        const int w = s_work;
+        __syncthreads();
+        if (w >= nwork) break;
+        const int u = w / Hkv, head = w % Hkv;
+        const int32_t* U = ws.units + (int64_t)u * UNIT_INTS;
+        const int q_lo = U[0], q_hi = U[1], t0u = U[2], t1u = U[3], ord = U[4];
+        const int R = (q_hi - q_lo + 1) * G;
+        const int32_t* tab = table_row(c, layer, slots[q_lo]);
+        for (int idx = tid; idx < R * D; idx += UNIT_THREADS) {
+            const int r = idx / D, d = idx % D;
+            const int seq = q_lo + r / G, g = r % G;
+            q_s[r][d] = Elem<T>::to_f(q[(int64_t)seq * q_stride + (int64_t)(head * G + g) * D + d]) * qscale;
+        }
+        if (tid < MAX_ROWS) {
+            m_s[tid] = -INFINITY;
+            l_s[tid] = 0.f;
+        }
+        float acc[MAX_ROWS];
+#pragma unroll
+        for (int r = 0; r < MAX_ROWS; ++r) acc[r] = 0.f;
+        const int d_own = tid % D, ts_own = tid / D;
+        for (int t0 = t0u; t0 < t1u; t0 += TT) {
+            const int cnt = min(TT, t1u - t0);
+            __syncthreads();
+            for (int idx = tid; idx < cnt * D; idx += UNIT_THREADS) {
+                const int j = idx / D, d = idx % D;
+                const int p = t0 + j;
+                const int64_t off = pool_row(c, layer, tab[p / bs], p % bs) + (int64_t)head * D + d;
+                k_s[j][d] = Elem<T>::to_f(kpool[off]);
+                v_s[j][d] = Elem<T>::to_f(vpool[off]);
+            }
+            __syncthreads();
+            {  // scores: lane = token, warps stride the rows
+                const int j = lane;
+                for (int r = warp; r < R; r += UNIT_THREADS / 32) {
+                    float s = -INFINITY;
+                    if (j < cnt) {
+                        s = 0.f;
+#pragma unroll 8
+                        for (int d = 0; d < D; ++d) s = fmaf(q_s[r][d], k_s[j][d], s);
+                    }
+                    float mx = s;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const float m_old = m_s[r];
+                    const float m_new = fmaxf(m_old, mx);
+                    const float p = (j < cnt) ? exp2f(s - m_new) : 0.f;
+                    float sum = p;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                    p_s[r][j] = p;
+                    __syncwarp();
+                    if (lane == 0) {
+                        const float alpha = exp2f(m_old - m_new);
+                        a_s[r] = alpha;
+                        l_s[r] = l_s[r] * alpha + sum;
+                        m_s[r] = m_new;
+                    }
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < MAX_ROWS; ++r) {
+                if (r < R) {
+                    float a = acc[r] * a_s[r];
+                    for (int j = ts_own; j < cnt; j += TS) a = fmaf(p_s[r][j], v_s[j][d_own], a);
+                    acc[r] = a;
+                }
+            }
+        }
+        __syncthreads();
+        if (TS > 1) {
+#pragma unroll
+            for (int r = 0; r < MAX_ROWS; ++r)
+                if (r < R) red_s[TS > 1 ? ts_own : 0][TS > 1 ? r : 0][TS > 1 ? d_own : 0] = acc[r];
+            __syncthreads();
+        }
+        if (ts_own == 0) {
+#pragma unroll
+            for (int r = 0; r < MAX_ROWS; ++r) {
+                if (r < R) {
+                    float a = acc[r];
+#pragma unroll
+                    for (int t = 1; t < TS; ++t) a += red_s[t][TS > 1 ? r : 0][TS > 1 ? d_own : 0];
+                    const int seq = q_lo + r / G, hq = head * G + r % G;
+                    const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
+                    ws.part_o[pi * D + d_own] = a;
+                    if (d_own == 0) {
+                        ws.part_ml[pi * 2] = m_s[r];
+                        ws.part_ml[pi * 2 + 1] = l_s[r];
+                    }
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. merge
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void k_merge(int Hq, DecodeWs ws, int max_parts, T* __restrict__ out, int64_t out_stride) {
+    const int i = blockIdx.x, d = threadIdx.x;
+    const int P = ws.nparts[i];
+    for (int hq = blockIdx.y; hq < Hq; hq += gridDim.y) {
+        float m = -INFINITY;
+        for (int p = 0; p < P; ++p) m = fmaxf(m, ws.part_ml[(((int64_t)i * max_parts + p) * Hq + hq) * 2]);
+        float l = 0.f, o = 0.f;
+        for (int p = 0; p < P; ++p) {
+            const int64_t pi = ((int64_t)i * max_parts + p) * Hq + hq;
+            const float w = exp2f(ws.part_ml[pi * 2] - m);
+            l += ws.part_ml[pi * 2 + 1] * w;
+            o += ws.part_o[pi * D + d] * w;
+        }
+        const float r = (P > 0 && l > 0.f) ? o / l : 0.f;
+        out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
+    }
+}
+
+// optional per-launch stage timing (plan, units, merge) with CUDA events on
+// the launch stream; enabled by mentat_profile_enable
+constexpr int PROF_MAX = 4096;
+static cudaEvent_t g_prof_ev[4][PROF_MAX];
+static int g_prof_cap = 0, g_prof_n = 0;
+static bool g_prof_on = false;
+
+static inline void prof_mark(int stage, cudaStream_t s) {
+    if (g_prof_on && g_prof_n < g_prof_cap) cudaEventRecord(g_prof_ev[stage][g_prof_n], s);
+}
+
+static int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <typename T, int D>
+static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,
+                         int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
+                         int max_parts, cudaStream_t s) {
+    const int G = Hq / c->num_kv_heads;
+    prof_mark(0, s);
+    k_plan<<<1, 1024, 0, s>>>(*c, layer, slots, n, G, ws, max_parts);
+    MENTAT_CHECK_LAUNCH();
+    prof_mark(1, s);
+    const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
+    k_units<T, D><<<num_sms() * 4, UNIT_THREADS, 0, s>>>(*c, layer, slots, reinterpret_cast<const T*>(q), q_stride,
+                                                         Hq, qscale, ws, max_parts);
+    MENTAT_CHECK_LAUNCH();
+    prof_mark(2, s);
+    dim3 mg(n, Hq < 8 ? Hq : 8);
+    k_merge<T, D><<<mg, D, 0, s>>>(Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride);
+    MENTAT_CHECK_LAUNCH();
+    prof_mark(3, s);
+    if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;
+    return MENTAT_OK;
+}
+
+}  // namespace mentat
+
+using namespace mentat;
+
+extern "C" {
+
+int64_t mentat_decode_workspace_bytes(int32_t n, int32_t hq, int32_t d, int32_t max_parts) {
+    DecodeWs w;
+    int64_t total = 0;
+    ws_carve(nullptr, n, hq, d, max_parts, &w, &total);
+    return total;
+}
+
+int32_t mentat_decode_max_parts(int32_t n, int32_t max_len, int32_t block_size) {
+    (void)block_size;
+    return (max_len + CHUNK - 1) / CHUNK + n + 1;
+}
+
+int mentat_profile_enable(int32_t max_records) {
+    if (max_records < 0 || max_records > PROF_MAX) return MENTAT_ERR_ARG;
+    for (int st = 0; st < 4; ++st)
+        for (int i = g_prof_cap; i < max_records; ++i)
+            if (cudaEventCreate(&g_prof_ev[st][i]) != cudaSuccess) return MENTAT_ERR_CUDA;
+    if (max_records > g_prof_cap) g_prof_cap = max_records;
+    g_prof_n = 0;
+    g_prof_on = max_records > 0;
+    return MENTAT_OK;
+}
+
+int mentat_profile_collect(double* stage_ms, int32_t* launches) {
+    if (!stage_ms || !launches) return MENTAT_ERR_ARG;
+    stage_ms[0] = stage_ms[1] = stage_ms[2] = 0.0;
+    *launches = g_prof_n;
+    if (g_prof_n > 0 && cudaEventSynchronize(g_prof_ev[3][g_prof_n - 1]) != cudaSuccess) return MENTAT_ERR_CUDA;
+    for (int i = 0; i < g_prof_n; ++i)
+        for (int st = 0; st < 3; ++st) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, g_prof_ev[st][i], g_prof_ev[st + 1][i]) != cudaSuccess) return MENTAT_ERR_CUDA;
+            stage_ms[st] += ms;
+        }
+    g_prof_n = 0;
+    return MENTAT_OK;
+}
+
+int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n, const void* q,
+                        int64_t q_stride, int32_t Hq, void* out, int64_t out_stride, float scale, void* workspace,
+                        int64_t ws_bytes, int32_t max_parts, cudaStream_t s) {
+    if (!c || layer < 0 || layer >= c->num_layers || n < 0 || n > PLAN_MAX_SEQS || !c->k_pool || !c->v_pool ||
+        Hq <= 0 || c->num_kv_heads <= 0 || Hq % c->num_kv_heads || max_parts <= 0)
+        return MENTAT_ERR_ARG;
+    if (n == 0) return MENTAT_OK;
+    if (!slots || !q || !out || !workspace) return MENTAT_ERR_ARG;
+    const int G = Hq / c->num_kv_heads;
+    if (G > MAX_ROWS) return MENTAT_ERR_UNSUPPORTED;
+    DecodeWs w;
+    int64_t need = 0;
+    ws_carve(workspace, n, Hq, c->head_dim, max_parts, &w, &need);
+    if (ws_bytes < need) return MENTAT_ERR_ARG;
+    const int D = c->head_dim;
+#define MENTAT_DISPATCH(T)                                                                                  \
+    if (D == 128)                                                                                           \
+        return launch_decode<T, 128>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts, s); \
+    if (D == 64)                                                                                            \
+        return launch_decode<T, 64>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts, s);  \
+    return MENTAT_ERR_UNSUPPORTED;
+    switch (c->dtype) {
+        case MENTAT_F32: { MENTAT_DISPATCH(float) }
+        case MENTAT_BF16: { MENTAT_DISPATCH(__nv_bfloat16) }
+        case MENTAT_F16: { MENTAT_DISPATCH(__half) }
+        default: return MENTAT_ERR_UNSUPPORTED;
+    }
+#undef MENTAT_DISPATCH
+}
+
+}  // extern "C"

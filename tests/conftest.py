@@ -12,6 +12,12 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
 
 
+def pytest_sessionstart(session):
+    # the C-ABI library is built in-tree; build it here if it is missing or stale
+    from mentat_b200 import build as _build
+    _build.build()
+
+
 @pytest.fixture(scope="session")
 def golden_dir():
     return os.path.join(ROOT, "tests", "golden")
