@@ -1,0 +1,344 @@
+"""Benchmark of the tree-aware paged decode attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mentat|reference]
+
+Workload: bf16, 32 q / 8 kv heads, head_dim 128, KV
+block 16; one 32768-token shared prefix and 64 branches with suffixes drawn
+from U[1024, 4096] (seeded).  A step is one ``attn_decode`` over the 64
+branches (plan + units + merge kernels).  The unique KV of a step (~0.8 GB) is
+larger than the 126 MB L2, so no flush is needed between steps.
+
+metric: decode-attn unique-KV HBM GB/s = distinct physical blocks' valid
+tokens x Hkv x D x 2 (K, V) x 2 B per step / step time; the whole-job
+aggregate over ranks (each rank decodes its own tree: weak scaling, no
+collective on the data path).
+
+``--impl reference`` times the reference's CPU path (oracle/cpu_path.py: the
+reference's build_packed_kv + _sdpa_decode restated with the same torch CPU
+ops) on the host cores, on a bounded sample of the same tree.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D, BS = 32, 8, 128, 16
+PREFIX, NBR, SUF_LO, SUF_HI = 32768, 64, 1024, 4096
+ELEM = 2
+METRIC = "decode-attn unique-KV HBM GB/s"
+
+
+def _env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def suffixes(seed):
+    return np.random.default_rng(seed).integers(SUF_LO, SUF_HI + 1, NBR)
+
+
+def unique_bytes(prefix, suffix_tokens):
+    return int((prefix + int(np.sum(suffix_tokens))) * HKV * D * 2 * ELEM)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class Clocks:
+    """nvidia-smi sampler running while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(self.gpu_id)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_tree(seed, device, extra_blocks):
+    from mentat_b200 import PagedKVCacheManager
+    suf = suffixes(seed)
+    blocks = PREFIX // BS + int(sum((s + BS - 1) // BS for s in suf)) + extra_blocks + 16
+    m = PagedKVCacheManager(1, HKV, D, max_blocks=blocks, block_size=BS, device=device, dtype=torch.bfloat16,
+                            max_seqs=NBR + 2)
+    g = torch.Generator(device=device).manual_seed(seed)
+    kv = lambda n: torch.randn((n, HKV, D), generator=g, device=device).to(torch.bfloat16)  # noqa: E731
+    root = m.allocate_sequence()
+    for a in range(0, PREFIX, 8192):
+        n = min(8192, PREFIX - a)
+        m.append_tokens(root, 0, kv(n), kv(n))
+    kids = [m.fork_sequence(root) for _ in range(NBR)]
+    m.free_sequence(root)
+    for kid, n in zip(kids, suf):
+        m.append_tokens(kid, 0, kv(int(n)), kv(int(n)))
+    q = torch.randn((NBR, HQ, D), generator=g, device=device).to(torch.bfloat16)
+    m.check()
+    return m, kids, q, suf
+
+
+def _cpu_inputs(m, kids, q, nbranch):
+    sel = kids[:nbranch]
+    tables = [m.page_table(s, 0) for s in sel]
+    lens = [m.get_kv_length(s) for s in sel]
+    return q[:nbranch].cpu(), m.k_pools[0].cpu(), m.v_pools[0].cpu(), tables, lens
+
+
+def cpu_sample(m, kids, q, nbranch, budget_s, max_calls=50):
+    """Time the reference CPU path on the prefix + the first nbranch branches."""
+    from oracle.cpu_path import decode_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    qc, kp, vp, tables, lens = _cpu_inputs(m, kids, q, nbranch)
+    ub = unique_bytes(PREFIX, np.array(lens) - PREFIX)
+    decode_step(qc, kp, vp, tables, lens, BS)  # warm
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or (time.perf_counter() < t_end and len(times) < max_calls):
+        t = time.perf_counter()
+        decode_step(qc, kp, vp, tables, lens, BS)
+        times.append(time.perf_counter() - t)
+    per = statistics.median(times)
+    return {"value": round(ub / per / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"shared 32768-token prefix + {nbranch} of 64 branches ({sum(lens)} tokens gathered, {ub} "
+                      f"unique KV bytes), median of {len(times)} calls of oracle.cpu_path.decode_step (the "
+                      "reference's build_packed_kv + _sdpa_decode, bf16, torch CPU)",
+            "seconds_per_call": per}
+
+
+def run_reference(args):
+    rank, world, local = _env_rank()
+    if rank != 0:
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "reference", "unavailable": "the seeded tree is built on a CUDA device"}))
+        return
+    from oracle.cpu_path import decode_step
+    m, kids, q, suf = build_tree(args.seed, torch.device("cuda", local), 0)
+    torch.cuda.synchronize()
+    torch.set_num_threads(os.cpu_count() or 1)
+    cal = cpu_sample(m, kids, q, 1, 0.0)
+    nb = int(max(1, min(8, 150.0 / max(1, args.steps + args.warmup) / max(cal["seconds_per_call"], 1e-3))))
+    qc, kp, vp, tables, lens = _cpu_inputs(m, kids, q, nb)
+    ub = unique_bytes(PREFIX, np.array(lens) - PREFIX)
+    for _ in range(args.warmup):
+        decode_step(qc, kp, vp, tables, lens, BS)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        decode_step(qc, kp, vp, tables, lens, BS)
+    dt = (time.perf_counter() - t) / args.steps
+    val = round(ub / dt / 1e9, 4)
+    sample = (f"32768-token prefix + {nb} of 64 branches per step ({ub} unique KV bytes); reference CPU path "
+              "(build_packed_kv + _sdpa_decode) restated in oracle/cpu_path.py")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, BASELINE config 4 tree)",
+        "config": {"workload": f"config 4 sample: {sample}", "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_mentat(args):
+    import torch.distributed as dist
+    from mentat_b200 import _lib
+    from mentat_b200.attention_backend import attn_decode
+    rank, world, local = _env_rank()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    lib = _lib.load()
+    m, kids, q, suf = build_tree(args.seed + rank, device,
+                                 extra_blocks=NBR * ((args.steps + args.warmup) // BS + 2))
+    ub = unique_bytes(PREFIX, suf)
+    k, v, cu, mx = m.build_packed_kv(kids, 0)
+    for _ in range(args.warmup):
+        attn_decode(q, k, v, None, cu, mx, NBR)
+    torch.cuda.synchronize()
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        gpu_id = str(local)
+    clocks = Clocks(gpu_id)
+    clocks.start()
+    time.sleep(0.3)
+
+    # device-resident timing: one attn_decode per step
+    _lib.check(lib.mentat_profile_enable(min(args.steps, 4096)), "mentat_profile_enable")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        attn_decode(q, k, v, None, cu, mx, NBR)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    stage = (ctypes.c_double * 3)()
+    cnt = ctypes.c_int32()
+    _lib.check(lib.mentat_profile_collect(stage, ctypes.byref(cnt)), "mentat_profile_collect")
+    lib.mentat_profile_enable(0)
+    m.check()
+
+    # end to end through the public API: pinned host inputs in, result out, every step
+    g = torch.Generator().manual_seed(args.seed + 1000 + rank)
+    q_host = q.cpu().pin_memory()
+    kv_host = torch.randn((args.steps + args.warmup, 2, NBR, HKV, D), generator=g).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty((NBR, HQ, D), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        qd = q_host.to(device, non_blocking=True)
+        kvd = kv_host[i].to(device, non_blocking=True)
+        m.append_tokens_batched(kids, 0, kvd[0], kvd[1])
+        kk, vv, cuk, mxk = m.build_packed_kv(kids, 0)
+        o = attn_decode(qd, kk, vv, None, cuk, mxk, NBR)
+        out_host.copy_(o, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    base = sum(m.get_kv_length(s) for s in kids) - NBR * PREFIX
+    e2e_bytes = sum(unique_bytes(PREFIX, [base + NBR * (i + 1)]) for i in range(args.steps))
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for i in range(args.steps):
+        e2e_step(args.warmup + i)
+    a1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    e2e_ms = a0.elapsed_time(a1)
+    m.check()
+
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=device)
+    tot = torch.tensor([float(ub), float(e2e_bytes)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms_max, e2e_max = t.tolist()
+    ub_all, e2e_all = tot.tolist()
+    value = ub_all * args.steps / (ms_max / 1e3) / 1e9
+    e2e_val = e2e_all / (e2e_max / 1e3) / 1e9
+    n_prof = max(cnt.value, 1)
+    units_ms = stage[1] / n_prof
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = ub / (units_ms / 1e3) / 1e9 if units_ms > 0 else None
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cpu = cpu_sample(m, kids, q, 2, 12.0)
+            cpu.pop("seconds_per_call", None)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v, BASELINE config 4 tree per rank)",
+            "config": {"workload": "BASELINE config 4: bf16 Hq32/Hkv8/D128, block 16, 32768-token shared prefix "
+                                   "+ 64 branches x U[1024,4096]-token suffixes",
+                       "unique_kv_bytes_per_step_per_rank": ub, "global_batch": NBR * world,
+                       "parallelism": f"independent trees x{world}",
+                       "l2": "inputs larger than L2 (unique KV > 126 MB), no flush"},
+            "roofline": {"bound": "hbm", "kernel": "k_units (tree-aware decode units)",
+                         "achieved": round(achieved, 2) if achieved else None, "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
+                         "traffic": ncu_traffic().get("k_units_c4_bytes_per_launch"),
+                         "stage_ms_per_launch": {"plan": stage[0] / n_prof, "units": units_ms,
+                                                 "merge": stage[2] / n_prof}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(q_host.numel() * 2 + kv_host[0].numel() * 2),
+                    "d2h_bytes_per_step": int(out_host.numel() * 2),
+                    "path": "pinned H2D q + new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
+                            "D2H output"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mentat", choices=["mentat", "reference"])
+    ap.add_argument("--seed", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mentat(args)
+
+
+if __name__ == "__main__":
+    main()
