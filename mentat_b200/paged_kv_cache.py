@@ -315,6 +315,9 @@ class PagedKVCacheManager:
             tf += c
             w += c
         if nb > self.max_blocks_per_seq:
+            if self.max_blocks_per_seq >= self.max_blocks:
+                # one sequence cannot hold more distinct blocks than the pool has
+                raise RuntimeError(OUT_OF_BLOCKS_MSG.format(n=self.max_blocks))
             raise RuntimeError(f"PagedKVCache: sequence {seq.seq_id} needs {nb} blocks per layer, "
                                f"max_blocks_per_seq={self.max_blocks_per_seq}")
         seq.num_blocks[layer], seq.tokens_in_last_block[layer] = nb, tf

@@ -114,13 +114,15 @@ class OraclePagedKV:
     """
 
     def __init__(self, num_layers, num_kv_heads, head_dim, max_blocks=4096,
-                 block_size=16, dtype=np.float32, order=None, with_data=True):
+                 block_size=16, dtype=np.float32, order=None, with_data=True, elem_bytes=None):
         self.num_layers = num_layers
         self.num_key_value_heads = num_kv_heads
         self.head_dim = head_dim
         self.max_blocks = max_blocks
         self.block_size = block_size
         self.dtype = np.dtype(dtype)
+        # bytes per element for get_stats (numpy has no bf16: data may be held wider)
+        self.elem_bytes = elem_bytes or self.dtype.itemsize
         self.allocator = OracleBlockAllocator(max_blocks, order)
         self.with_data = with_data
         shape = (max_blocks, block_size, num_kv_heads, head_dim)
@@ -281,7 +283,7 @@ class OraclePagedKV:
         a = self.allocator
         total = sum(s.num_tokens[0] for s in self._sequences.values())
         bpb = (2 * self.num_layers * self.block_size * self.num_key_value_heads
-               * self.head_dim * self.dtype.itemsize)
+               * self.head_dim * self.elem_bytes)
         return {
             "num_sequences": len(self._sequences),
             "total_cached_tokens": total,

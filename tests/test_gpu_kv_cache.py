@@ -100,7 +100,7 @@ def test_decode_steps_append_batched_matches_oracle():
     order = rng.permutation(pool).tolist()
     m = PagedKVCacheManager(L, hkv, d, max_blocks=pool, block_size=bs, device="cuda", dtype=torch.bfloat16,
                             free_order=order, strict=True)
-    o = OraclePagedKV(L, hkv, d, pool, bs, order=order)
+    o = OraclePagedKV(L, hkv, d, pool, bs, order=order, elem_bytes=2)
     s = m.allocate_sequence()
     o.allocate_sequence()
     for layer in range(L):
@@ -157,10 +157,18 @@ def test_duplicate_slot_in_batch_is_sequential():
 
 
 def test_out_of_blocks_raises_reference_message():
+    """Found on the device (two sequences together exhaust the pool) and raised
+    with the reference's message at the next check."""
     from mentat_b200 import PagedKVCacheManager
-    m = PagedKVCacheManager(1, 1, 64, max_blocks=2, block_size=4, device="cuda", dtype=torch.float32)
-    s = m.allocate_sequence()
-    z = torch.zeros(12, 1, 64, device="cuda")
-    m.append_tokens(s, 0, z, z)  # needs 3 blocks of a 2-block pool
-    with pytest.raises(RuntimeError, match=r"out of blocks \(pool size=2\)"):
+    m = PagedKVCacheManager(1, 1, 64, max_blocks=3, block_size=4, device="cuda", dtype=torch.float32)
+    a, b = m.allocate_sequence(), m.allocate_sequence()
+    z = torch.zeros(8, 1, 64, device="cuda")
+    m.append_tokens(a, 0, z, z)  # 2 blocks
+    m.append_tokens(b, 0, z, z)  # 2 more blocks of a 3-block pool
+    with pytest.raises(RuntimeError, match=r"out of blocks \(pool size=3\)"):
         m.check()
+    # a single sequence larger than the pool is refused on the host, same message
+    m2 = PagedKVCacheManager(1, 1, 64, max_blocks=2, block_size=4, device="cuda", dtype=torch.float32)
+    s = m2.allocate_sequence()
+    with pytest.raises(RuntimeError, match=r"out of blocks \(pool size=2\)"):
+        m2.append_tokens(s, 0, torch.zeros(12, 1, 64, device="cuda"), torch.zeros(12, 1, 64, device="cuda"))
