@@ -144,6 +144,29 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
                         int64_t out_stride, float scale, void* workspace, int64_t workspace_bytes,
                         int32_t max_parts, cudaStream_t s);
 
+/* Decode for callers that cannot allocate device memory when they call.
+ * No counterpart in the reference.  Some hosts cannot hand this library a
+ * workspace: a program that binds the C ABI directly has no caching allocator,
+ * and a cudaMalloc per call would synchronise the whole device; a serving
+ * runtime may reserve all device memory up front and forbid new allocations
+ * while it serves.  This variant of mentat_paged_decode takes the same
+ * arguments minus the workspace and uses a fixed scratch array compiled into
+ * the library instead (MENTAT_NOALLOC_SCRATCH_BYTES, held on every GPU that
+ * loads the library until the process exits).  It never allocates.
+ *  - A request whose workspace (mentat_decode_workspace_bytes(n, num_q_heads,
+ *    head_dim, max_parts)) exceeds the limit returns MENTAT_ERR_SCRATCH_LIMIT
+ *    and launches nothing.
+ *  - The first call on a device looks up the array's device address with that
+ *    device current; make that first call before any stream capture.
+ *  - Every call on a device shares the one array, and each call overwrites it
+ *    (the plan resets its own counters): calls that overlap on the GPU, e.g. on
+ *    two streams, race and must be serialised by the caller. */
+#define MENTAT_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+#define MENTAT_ERR_SCRATCH_LIMIT (-4)
+int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
+                                const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
+                                int64_t out_stride, float scale, int32_t max_parts, cudaStream_t s);
+
 /* Stage timing of mentat_paged_decode (plan, units, merge) with CUDA events
  * recorded on the launch stream, for up to max_records launches (0 disables).
  * No counterpart in the reference; used by the benchmark's roofline report.

@@ -19,6 +19,8 @@ CTRL_HEAD, CTRL_TAIL, CTRL_PEAK, CTRL_ERROR, CTRL_ERRARG, CTRL_ALLOCS, CTRL_COWS
 CTRL_WORDS = 16
 DEV_OUT_OF_BLOCKS, DEV_REF_FREE, DEV_RELEASE_FREE, DEV_PLAN_OVERFLOW, DEV_TABLE_OVERFLOW = 1, 2, 3, 4, 5
 GATE_MAXK = 8
+NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
+ERR_SCRATCH_LIMIT = -4
 
 
 class KVCache(C.Structure):
@@ -68,6 +70,7 @@ SIGNATURES = [
     ("mentat_decode_workspace_bytes", _I64, [_I32, _I32, _I32, _I32]),
     ("mentat_decode_max_parts", _I32, [_I32, _I32, _I32]),
     ("mentat_paged_decode", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
+    ("mentat_paged_decode_noalloc", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _I32, _P]),
     ("mentat_profile_enable", C.c_int, [_I32]),
     ("mentat_profile_collect", C.c_int, [C.POINTER(C.c_double), C.POINTER(_I32)]),
     ("mentat_gate_step", C.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, C.POINTER(GateParams), _P, _P]),

@@ -492,3 +492,35 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode without a caller-provided workspace, for hosts that cannot allocate
+// device memory at call time.  The workspace lives in this fixed array; host
+// code must not pass the symbol itself to a kernel (on the host it is only a
+// stand-in), so its device address is looked up once per device.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MENTAT_NOALLOC_SCRATCH_BYTES];
+static void* g_noalloc_addr[64] = {nullptr};
+
+extern "C" int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
+                                           const void* q, int64_t q_stride, int32_t Hq, void* out, int64_t out_stride,
+                                           float scale, int32_t max_parts, cudaStream_t s) {
+    if (!c || Hq <= 0 || n < 0 || n > PLAN_MAX_SEQS || max_parts <= 0) return MENTAT_ERR_ARG;
+    const int64_t need = mentat_decode_workspace_bytes(n, Hq, c->head_dim, max_parts);
+    if (need > (int64_t)MENTAT_NOALLOC_SCRATCH_BYTES) return MENTAT_ERR_SCRATCH_LIMIT;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        (void)cudaGetLastError();
+        return MENTAT_ERR_CUDA;
+    }
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+            (void)cudaGetLastError();
+            return MENTAT_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    return mentat_paged_decode(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, g_noalloc_addr[dev],
+                               (int64_t)MENTAT_NOALLOC_SCRATCH_BYTES, max_parts, s);
+}

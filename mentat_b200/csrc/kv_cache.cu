@@ -531,6 +531,7 @@ const char* mentat_status_string(int s) {
         case MENTAT_ERR_ARG: return "invalid argument";
         case MENTAT_ERR_CUDA: return "CUDA launch failed";
         case MENTAT_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+        case MENTAT_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of the no-allocation entry point";
         case MENTAT_DEV_OUT_OF_BLOCKS: return "out of blocks";
         case MENTAT_DEV_REF_FREE: return "ref() on free block";
         case MENTAT_DEV_RELEASE_FREE: return "release() on free block";
