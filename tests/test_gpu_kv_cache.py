@@ -103,8 +103,8 @@ def test_decode_steps_append_batched_matches_oracle():
     o = OraclePagedKV(L, hkv, d, pool, bs, order=order, elem_bytes=2)
     s = m.allocate_sequence()
     o.allocate_sequence()
-    for layer in range(L):
-        kv = round_np(rng.standard_normal((7, hkv, d), dtype=np.float32), "bf16")
+    for layer in range(L):  # 6 + 1 tokens at the first fork: a shared partial tail, so CoW happens
+        kv = round_np(rng.standard_normal((6, hkv, d), dtype=np.float32), "bf16")
         t = torch.from_numpy(kv).cuda().bfloat16()
         m.append_tokens(s, layer, t, t)
         o.append_tokens(s, layer, kv, kv)
