@@ -237,7 +237,7 @@ def run_mentat(args):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    stage = (ctypes.c_double * 3)()
+    stage = (ctypes.c_double * 4)()
     cnt = ctypes.c_int32()
     _lib.check(lib.mentat_profile_collect(stage, ctypes.byref(cnt)), "mentat_profile_collect")
     lib.mentat_profile_enable(0)
@@ -284,11 +284,22 @@ def run_mentat(args):
     value = ub_all * args.steps / (ms_max / 1e3) / 1e9
     e2e_val = e2e_all / (e2e_max / 1e3) / 1e9
     n_prof = max(cnt.value, 1)
-    units_ms = stage[1] / n_prof
+    st_ms = {"plan": stage[0] / n_prof, "units_ffma": stage[1] / n_prof, "units_tc": stage[2] / n_prof,
+             "merge": stage[3] / n_prof}
+    # bytes each unit kernel streams: the shared prefix goes to the tensor-core units
+    # (64 branches x 4 query heads >= 16 rows), the branch suffixes to the FFMA units
+    shared_b = unique_bytes(PREFIX, [0])
+    dom = "units_tc" if st_ms["units_tc"] >= st_ms["units_ffma"] else "units_ffma"
+    dom_bytes = shared_b if dom == "units_tc" else ub - shared_b
+    units_ms = st_ms[dom]
 
     if rank == 0:
         peak, peak_kind = peaks()
-        achieved = ub / (units_ms / 1e3) / 1e9 if units_ms > 0 else None
+        achieved = dom_bytes / (units_ms / 1e3) / 1e9 if units_ms > 0 else None
+        kernels = {"k_units_tc": {"bytes": shared_b, "ms": st_ms["units_tc"]},
+                   "k_units (FFMA)": {"bytes": ub - shared_b, "ms": st_ms["units_ffma"]}}
+        for kv in kernels.values():
+            kv["GBps"] = round(kv["bytes"] / (kv["ms"] / 1e3) / 1e9, 1) if kv["ms"] > 0 else None
         cpu = None
         if world == 1 and not args.no_cpu:
             cpu = cpu_sample(m, kids, q, 2, 12.0)
@@ -303,19 +314,20 @@ def run_mentat(args):
                        "unique_kv_bytes_per_step_per_rank": ub, "global_batch": NBR * world,
                        "parallelism": f"independent trees x{world}",
                        "l2": "inputs larger than L2 (unique KV > 126 MB), no flush"},
-            "roofline": {"bound": "hbm", "kernel": "k_units (tree-aware decode units)",
+            "roofline": {"bound": "hbm", "kernel": {"units_tc": "k_units_tc", "units_ffma": "k_units"}[dom],
                          "achieved": round(achieved, 2) if achieved else None, "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": ncu_traffic().get("k_units_c4_bytes_per_launch"),
-                         "stage_ms_per_launch": {"plan": stage[0] / n_prof, "units": units_ms,
-                                                 "merge": stage[2] / n_prof}},
+                         "traffic": ncu_traffic().get(f"{dom}_c4_bytes_per_launch"),
+                         "stage_ms_per_launch": st_ms, "per_kernel": kernels,
+                         "whole_call": {"bytes": ub, "ms": ms_max / args.steps,
+                                        "GBps": round(ub / (ms_max / args.steps / 1e3) / 1e9, 1)}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(q_host.numel() * 2 + kv_host[0].numel() * 2),
                     "d2h_bytes_per_step": int(out_host.numel() * 2),
                     "path": "pinned H2D q + new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
                             "D2H output"},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 4 * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

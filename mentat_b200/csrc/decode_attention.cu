@@ -18,18 +18,25 @@
 
 #include "common.cuh"
 
+#include <cstdlib>
+#include <type_traits>
+
 namespace mentat {
 
-constexpr int PLAN_HDR = 64;        // ints: [0] units, [1] work counter, [2] error
+constexpr int PLAN_HDR = 64;        // header ints, see HDR_*
+constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC_NEXT = 4, HDR_TC_ABORT = 5;
 constexpr int UNIT_INTS = 8;        // seq_lo, seq_hi, tok0, tok1, ordinal
-constexpr int CHUNK = 256;          // tokens per unit
+constexpr int CHUNK = 256;          // tokens per FFMA unit
+constexpr int CHUNK_TC = 1024;      // tokens per tensor-core unit
 constexpr int MAX_ROWS = 16;        // query rows per unit on the FFMA path
+constexpr int TC_MAX_ROWS = 256;    // query rows per unit on the tensor-core path (two M=128 tiles)
 constexpr int PLAN_MAX_SEQS = 512;  // sequences per launch (callers split larger batches)
 
 struct DecodeWs {
     int32_t* hdr;
     int32_t* nparts;  // [n]
-    int32_t* units;   // [n * max_parts][UNIT_INTS]
+    int32_t* units;   // [n * max_parts][UNIT_INTS]  FFMA units
+    int32_t* units_tc;  // [n * max_parts][UNIT_INTS]  tensor-core units
     float* part_ml;   // [n][max_parts][Hq][2]
     float* part_o;    // [n][max_parts][Hq][D]
 };
@@ -48,6 +55,7 @@ __host__ __device__ inline void ws_carve(void* base, int n, int hq, int d, int m
     w->hdr = reinterpret_cast<int32_t*>(take(PLAN_HDR * 4));
     w->nparts = reinterpret_cast<int32_t*>(take((int64_t)n * 4));
     w->units = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
+    w->units_tc = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
     w->part_ml = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * 2 * 4));
     w->part_o = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * d * 4));
     *total = off;
@@ -56,8 +64,26 @@ __host__ __device__ inline void ws_carve(void* base, int n, int hq, int d, int m
 // ---------------------------------------------------------------------------
 // 1. plan
 // ---------------------------------------------------------------------------
+// Plan parameters for one launch.  A segment (node of the LCP-interval tree or
+// a sequence's own leaf range) with rows = width x G goes to the tensor-core
+// unit kernel when tc_min_rows <= rows (and the layout supports it), else to
+// the FFMA kernel.
+struct PlanParams {
+    int G;
+    int tc_ok;        // dtype / head_dim / block size fit the tensor-core kernel
+    int tc_min_rows;  // rows threshold for the tensor-core kernel
+};
+
+__device__ __forceinline__ bool seg_is_tc(const PlanParams& pp, int width) {
+    return pp.tc_ok && width * pp.G >= pp.tc_min_rows;
+}
+__device__ __forceinline__ int seg_chunk(bool tc) { return tc ? CHUNK_TC : CHUNK; }
+__device__ __forceinline__ int seg_spu(const PlanParams& pp, bool tc) {
+    return max(1, (tc ? TC_MAX_ROWS : MAX_ROWS) / pp.G);
+}
+
 __global__ void __launch_bounds__(1024)
-k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeWs ws, int max_parts) {
+k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp, DecodeWs ws, int max_parts) {
     __shared__ int s_len[PLAN_MAX_SEQS];
     __shared__ int s_slot[PLAN_MAX_SEQS];
     __shared__ int s_h[PLAN_MAX_SEQS + 1];    // h[i] = LCP(i-1, i) in tokens, h[0] = h[n] = 0
@@ -66,7 +92,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeW
     __shared__ int s_post[PLAN_MAX_SEQS];     // node ids in pop (post) order
     __shared__ int s_nbase[PLAN_MAX_SEQS], s_nchunk[PLAN_MAX_SEQS];
     __shared__ int s_seg_units[2 * PLAN_MAX_SEQS];  // internal nodes, then leaves
-    __shared__ int s_seg_first[2 * PLAN_MAX_SEQS];
+    __shared__ int s_seg_first[2 * PLAN_MAX_SEQS];  // first FFMA unit of each segment
+    __shared__ int s_seg_first_tc[2 * PLAN_MAX_SEQS];  // first tensor-core unit of each segment
     __shared__ int smem32[32];
     __shared__ int s_nnodes, s_err;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -145,17 +172,20 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeW
             const int x = s_post[k];
             const int p = s_npar[x];
             const int pdep = p >= 0 ? s_ndep[p] : 0;
-            s_nchunk[x] = (s_ndep[x] - pdep + CHUNK - 1) / CHUNK;
+            const int ch = seg_chunk(seg_is_tc(pp, s_nhi[x] - s_nlo[x] + 1));
+            s_nchunk[x] = (s_ndep[x] - pdep + ch - 1) / ch;
             s_nbase[x] = p >= 0 ? s_nbase[p] + s_nchunk[p] : 0;
         }
     }
     __syncthreads();
     const int nn = s_nnodes;
-    const int spu = max(1, MAX_ROWS / G);  // sequences per unit
-    for (int s = tid; s < nn + n; s += blockDim.x) {
+    const int nseg = nn + n;
+    const bool leaf_tc = seg_is_tc(pp, 1);
+    for (int s = tid; s < nseg; s += blockDim.x) {
         int cnt;
         if (s < nn) {
             const int width = s_nhi[s] - s_nlo[s] + 1;
+            const int spu = seg_spu(pp, seg_is_tc(pp, width));
             cnt = s_nchunk[s] * ((width + spu - 1) / spu);
         } else {
             const int i = s - nn;
@@ -164,7 +194,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeW
             const int node = da >= db ? a : b;
             const int d0 = node >= 0 ? s_ndep[node] : 0;
             const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
-            const int ch = (s_len[i] - d0 + CHUNK - 1) / CHUNK;
+            const int chunk = seg_chunk(leaf_tc);
+            const int ch = (s_len[i] - d0 + chunk - 1) / chunk;
             cnt = ch;
             ws.nparts[i] = base + ch;
             if (base + ch > max_parts) atomicExch(&s_err, 1);
@@ -172,41 +203,59 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeW
         s_seg_units[s] = cnt;
     }
     __syncthreads();
+    // exclusive scans of the unit counts, separately per kernel kind
+    const int s0 = 2 * tid, s1 = 2 * tid + 1;
+    auto is_tc_seg = [&](int s) { return s < nn ? seg_is_tc(pp, s_nhi[s] - s_nlo[s] + 1) : leaf_tc; };
+    int total_simt, total_tc;
     {
-        const int s0 = 2 * tid, s1 = 2 * tid + 1;
-        const int c0 = s0 < nn + n ? s_seg_units[s0] : 0;
-        const int c1 = s1 < nn + n ? s_seg_units[s1] : 0;
-        int total;
-        const int e = block_exclusive_scan(c0 + c1, &total, smem32);
-        if (s0 < nn + n) s_seg_first[s0] = e;
-        if (s1 < nn + n) s_seg_first[s1] = e + c0;
-        if (tid == 0) {
-            if ((int64_t)total > (int64_t)n * max_parts) s_err = 1;
-            ws.hdr[0] = s_err ? 0 : total;
-            ws.hdr[1] = 0;
-            ws.hdr[2] = s_err;
-            if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, total);
-        }
-        __syncthreads();
-        if (s_err) return;
+        const int c0 = (s0 < nseg && !is_tc_seg(s0)) ? s_seg_units[s0] : 0;
+        const int c1 = (s1 < nseg && !is_tc_seg(s1)) ? s_seg_units[s1] : 0;
+        const int e = block_exclusive_scan(c0 + c1, &total_simt, smem32);
+        if (s0 < nseg) s_seg_first[s0] = e;
+        if (s1 < nseg) s_seg_first[s1] = e + c0;
+    }
+    {
+        const int c0 = (s0 < nseg && is_tc_seg(s0)) ? s_seg_units[s0] : 0;
+        const int c1 = (s1 < nseg && is_tc_seg(s1)) ? s_seg_units[s1] : 0;
+        const int e = block_exclusive_scan(c0 + c1, &total_tc, smem32);
+        if (s0 < nseg) s_seg_first_tc[s0] = e;
+        if (s1 < nseg) s_seg_first_tc[s1] = e + c0;
+    }
+    if (tid == 0) {
+        if ((int64_t)total_simt > (int64_t)n * max_parts || (int64_t)total_tc > (int64_t)n * max_parts) s_err = 1;
+        ws.hdr[HDR_NSIMT] = s_err ? 0 : total_simt;
+        ws.hdr[HDR_SIMT_NEXT] = 0;
+        ws.hdr[HDR_ERR] = s_err;
+        ws.hdr[HDR_NTC] = s_err ? 0 : total_tc;
+        ws.hdr[HDR_TC_NEXT] = 0;
+        if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, total_simt + total_tc);
+    }
+    __syncthreads();
+    if (s_err) return;
+    for (int kind = 0; kind < 2; ++kind) {
+        const int total = kind ? total_tc : total_simt;
+        const int* first = kind ? s_seg_first_tc : s_seg_first;
+        int32_t* units = kind ? ws.units_tc : ws.units;
         for (int u = tid; u < total; u += blockDim.x) {
-            int lo = 0, hi = nn + n - 1;  // last segment whose first unit <= u
+            int lo = 0, hi = nseg - 1;  // last segment whose first unit <= u (zero-count segments precede it)
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
-                if (s_seg_first[mid] <= u) lo = mid; else hi = mid - 1;
+                if (first[mid] <= u) lo = mid; else hi = mid - 1;
             }
-            const int s = lo, k = u - s_seg_first[s];
+            const int s = lo, k = u - first[s];
             int q_lo, q_hi, t0, t1, ord;
             if (s < nn) {
                 const int width = s_nhi[s] - s_nlo[s] + 1;
+                const bool tc = seg_is_tc(pp, width);
+                const int spu = seg_spu(pp, tc), chunk = seg_chunk(tc);
                 const int ngroups = (width + spu - 1) / spu;
                 const int ch = k / ngroups, rg = k % ngroups;
                 const int p = s_npar[s];
                 const int pdep = p >= 0 ? s_ndep[p] : 0;
                 q_lo = s_nlo[s] + rg * spu;
                 q_hi = min(s_nhi[s], q_lo + spu - 1);
-                t0 = pdep + ch * CHUNK;
-                t1 = min(s_ndep[s], t0 + CHUNK);
+                t0 = pdep + ch * chunk;
+                t1 = min(s_ndep[s], t0 + chunk);
                 ord = s_nbase[s] + ch;
             } else {
                 const int i = s - nn;
@@ -215,12 +264,13 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, int G, DecodeW
                 const int node = da >= db ? a : b;
                 const int d0 = node >= 0 ? s_ndep[node] : 0;
                 const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
+                const int chunk = seg_chunk(leaf_tc);
                 q_lo = q_hi = i;
-                t0 = d0 + k * CHUNK;
-                t1 = min(s_len[i], t0 + CHUNK);
+                t0 = d0 + k * chunk;
+                t1 = min(s_len[i], t0 + chunk);
                 ord = base + k;
             }
-            int32_t* U = ws.units + (int64_t)u * UNIT_INTS;
+            int32_t* U = units + (int64_t)u * UNIT_INTS;
             U[0] = q_lo; U[1] = q_hi; U[2] = t0; U[3] = t1; U[4] = ord;
         }
     }
@@ -247,12 +297,12 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
     __shared__ int s_work;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hkv = c.num_kv_heads, G = Hq / Hkv, bs = c.block_size;
-    const int nunits = ws.hdr[0];
+    const int nunits = ws.hdr[HDR_NSIMT];
     const int64_t nwork = (int64_t)nunits * Hkv;
     const T* kpool = reinterpret_cast<const T*>(c.k_pool);
     const T* vpool = reinterpret_cast<const T*>(c.v_pool);
     for (;;) {
-        if (tid == 0) s_work = atomicAdd(&ws.hdr[1], 1);
+        if (tid == 0) s_work = atomicAdd(&ws.hdr[HDR_SIMT_NEXT], 1);
         __syncthreads();
         const int w = s_work;
         __syncthreads();
@@ -373,10 +423,17 @@ __global__ void k_merge(int Hq, DecodeWs ws, int max_parts, T* __restrict__ out,
     }
 }
 
-// optional per-launch stage timing (plan, units, merge) with CUDA events on
-// the launch stream; enabled by mentat_profile_enable
+}  // namespace mentat
+
+#include "decode_tc.cuh"
+
+namespace mentat {
+
+// optional per-launch stage timing (plan, FFMA units, tensor-core units,
+// merge) with CUDA events on the launch stream; enabled by mentat_profile_enable
+constexpr int PROF_STAGES = 4;
 constexpr int PROF_MAX = 4096;
-static cudaEvent_t g_prof_ev[4][PROF_MAX];
+static cudaEvent_t g_prof_ev[PROF_STAGES + 1][PROF_MAX];
 static int g_prof_cap = 0, g_prof_n = 0;
 static bool g_prof_on = false;
 
@@ -395,13 +452,42 @@ static int num_sms() {
     return n;
 }
 
+// rows at or above which a shared segment goes to the tensor-core kernel
+// (MENTAT_TC_MIN_ROWS overrides; a value above 256 disables the tensor-core path)
+static int tc_min_rows() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MENTAT_TC_MIN_ROWS");
+        v = (e && *e) ? atoi(e) : 16;
+        if (v < 1) v = 1;
+    }
+    return v;
+}
+
 template <typename T, int D>
 static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,
                          int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
                          int max_parts, cudaStream_t s) {
     const int G = Hq / c->num_kv_heads;
+    const PoolMaps* maps = nullptr;
+    bool tc_ok = false;
+    if constexpr (!std::is_same<T, float>::value) {
+        tc_ok = tc_supported(c) && tc_min_rows() <= TC_MAX_ROWS && ((uintptr_t)q % 16 == 0) && (q_stride % 8 == 0);
+        if (tc_ok) {
+            maps = pool_maps(c, layer);
+            tc_ok = maps != nullptr;
+        }
+        static bool attr = false;
+        if (tc_ok && !attr) {
+            if (cudaFuncSetAttribute(k_units_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
+                cudaSuccess)
+                return MENTAT_ERR_CUDA;
+            attr = true;
+        }
+    }
+    PlanParams pp{G, tc_ok ? 1 : 0, tc_min_rows()};
     prof_mark(0, s);
-    k_plan<<<1, 1024, 0, s>>>(*c, layer, slots, n, G, ws, max_parts);
+    k_plan<<<1, 1024, 0, s>>>(*c, layer, slots, n, pp, ws, max_parts);
     MENTAT_CHECK_LAUNCH();
     prof_mark(1, s);
     const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
@@ -409,10 +495,19 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
                                                          Hq, qscale, ws, max_parts);
     MENTAT_CHECK_LAUNCH();
     prof_mark(2, s);
+    if constexpr (!std::is_same<T, float>::value) {
+        if (tc_ok) {
+            k_units_tc<T, D><<<num_sms(), TC_THREADS, TC_SMEM, s>>>(maps->mk, maps->mv, *c, layer, slots,
+                                                                    reinterpret_cast<const T*>(q), q_stride, Hq,
+                                                                    qscale, ws, max_parts);
+            MENTAT_CHECK_LAUNCH();
+        }
+    }
+    prof_mark(3, s);
     dim3 mg(n, Hq < 8 ? Hq : 8);
     k_merge<T, D><<<mg, D, 0, s>>>(Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride);
     MENTAT_CHECK_LAUNCH();
-    prof_mark(3, s);
+    prof_mark(4, s);
     if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;
     return MENTAT_OK;
 }
@@ -437,7 +532,7 @@ int32_t mentat_decode_max_parts(int32_t n, int32_t max_len, int32_t block_size) 
 
 int mentat_profile_enable(int32_t max_records) {
     if (max_records < 0 || max_records > PROF_MAX) return MENTAT_ERR_ARG;
-    for (int st = 0; st < 4; ++st)
+    for (int st = 0; st <= PROF_STAGES; ++st)
         for (int i = g_prof_cap; i < max_records; ++i)
             if (cudaEventCreate(&g_prof_ev[st][i]) != cudaSuccess) return MENTAT_ERR_CUDA;
     if (max_records > g_prof_cap) g_prof_cap = max_records;
@@ -448,11 +543,12 @@ int mentat_profile_enable(int32_t max_records) {
 
 int mentat_profile_collect(double* stage_ms, int32_t* launches) {
     if (!stage_ms || !launches) return MENTAT_ERR_ARG;
-    stage_ms[0] = stage_ms[1] = stage_ms[2] = 0.0;
+    for (int st = 0; st < PROF_STAGES; ++st) stage_ms[st] = 0.0;
     *launches = g_prof_n;
-    if (g_prof_n > 0 && cudaEventSynchronize(g_prof_ev[3][g_prof_n - 1]) != cudaSuccess) return MENTAT_ERR_CUDA;
+    if (g_prof_n > 0 && cudaEventSynchronize(g_prof_ev[PROF_STAGES][g_prof_n - 1]) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
     for (int i = 0; i < g_prof_n; ++i)
-        for (int st = 0; st < 3; ++st) {
+        for (int st = 0; st < PROF_STAGES; ++st) {
             float ms = 0.f;
             if (cudaEventElapsedTime(&ms, g_prof_ev[st][i], g_prof_ev[st + 1][i]) != cudaSuccess) return MENTAT_ERR_CUDA;
             stage_ms[st] += ms;

@@ -1,0 +1,481 @@
+// Tensor-core (tcgen05) decode units for bf16 / fp16 caches, head_dim 64 or 128,
+// KV block 16.  Included by decode_attention.cu; consumes the plan's
+// tensor-core unit queue (segments with >= tc_min_rows query rows: the shared
+// prefixes of a tree).
+//
+// One CTA per SM (persistent, 4 warps, ~193 KB of shared memory).  Per unit and
+// kv head:
+//   * Q rows of all sharing sequences (up to 256 = two M=128 row tiles) are
+//     written once to shared memory in the K-major 128-byte-swizzled layout.
+//   * K and V come in 64-token tiles (4 blocks) by TMA from the paged pool,
+//     through a 3-stage mbarrier ring, each (block, head) box read once for
+//     every row of the unit.
+//   * S = Q K^T: tcgen05.mma kind::f16, M=128, N=64, K=head_dim, accumulator
+//     in TMEM.  Each thread owns one query row (TMEM lane): scale, mask, online
+//     softmax in base 2 with a lazily raised reference max (O is rescaled in
+//     TMEM only when the row max grows by more than 2^8), P rounded to the
+//     cache dtype and written K-major swizzled to shared memory.
+//   * O += P V: tcgen05.mma, M=128, N=head_dim, K=64 tokens, V read MN-major.
+//   * The unnormalised (m, l, o) partial goes to the workspace like the FFMA
+//     units, and k_merge combines both kinds.
+// Every mbarrier wait is bounded by a clock limit; on timeout the CTA records
+// HDR_TC_ABORT, stops issuing work, drains its outstanding copies (bounded) and
+// frees its TMEM before returning.
+
+#pragma once
+
+#include <cuda.h>
+
+namespace mentat {
+
+constexpr int TC_THREADS = 128;
+constexpr int TC_TILE = 64;                 // tokens per K/V tile (4 blocks of 16)
+constexpr int TC_NST = 3;                   // K/V pipeline stages
+constexpr int TC_RT = 2;                    // row tiles (128 rows each)
+constexpr int TC_Q_BYTES = TC_RT * 2 * 128 * 128;          // 64 KB: [rt][half][128 rows][128 B]
+constexpr int TC_KV_STAGE = 2 * TC_TILE * 128;              // 16 KB: [half][64 tok][128 B]
+constexpr int TC_P_BYTES = TC_RT * 128 * 128;               // 32 KB: [rt][128 rows][128 B]
+constexpr int TC_OFF_Q = 0;
+constexpr int TC_OFF_K = TC_OFF_Q + TC_Q_BYTES;
+constexpr int TC_OFF_V = TC_OFF_K + TC_NST * TC_KV_STAGE;
+constexpr int TC_OFF_P = TC_OFF_V + TC_NST * TC_KV_STAGE;
+constexpr int TC_OFF_BAR = TC_OFF_P + TC_P_BYTES;           // mbarriers: full[NST], mma
+constexpr int TC_SMEM = TC_OFF_BAR + 128 + 1024;            // + alignment slack
+constexpr uint32_t TC_TMEM_COLS = 512;      // O[rt] at rt*128, S[rt] at 256 + rt*64
+constexpr long long TC_WAIT_CYCLES = 4000000000ll;  // ~2 s at 1.9 GHz
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait: false on timeout
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > TC_WAIT_CYCLES) return false;
+    }
+    return true;
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem], kind::f16, one thread issues
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// shared-memory matrix descriptor, 128-byte swizzle (Blackwell version 1)
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;  // version
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+// instruction descriptor, kind::f16, fp32 accumulate
+__host__ __device__ constexpr uint32_t idesc_f16(int fmt, int m, int n, int a_mn_major, int b_mn_major) {
+    return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)a_mn_major << 15) |
+           ((uint32_t)b_mn_major << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+// byte offset of (row, 16-byte chunk) in a K-major 128B-swizzled [rows][128 B] region
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
+    return (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u + (uint32_t)((chunk ^ (row & 7)) << 4);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+           mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict__ q, int64_t q_stride, int Hq,
+           float scale_log2, DecodeWs ws, int max_parts) {
+    constexpr int HALVES = D / 64;                // 128-byte column halves of a row
+    constexpr int FMT = Elem<T>::code == MENTAT_BF16 ? 1 : 0;
+    constexpr uint32_t IDESC_QK = idesc_f16(FMT, 128, TC_TILE, 0, 0);
+    constexpr uint32_t IDESC_PV = idesc_f16(FMT, 128, D, 0, 1);
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_work, s_abort;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar_full0 = sbase + TC_OFF_BAR;
+    const uint32_t bar_mma = sbase + TC_OFF_BAR + 8 * TC_NST;
+    const int Hkv = c.num_kv_heads, G = Hq / Hkv;
+
+    // zero Q / K / V / P once: padded rows and unloaded tokens must be finite
+    for (int i = tid; i < TC_OFF_BAR / 16; i += TC_THREADS) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    if (tid == 0) {
+        for (int st = 0; st < TC_NST; ++st) mbar_init(bar_full0 + 8 * st, 1);
+        mbar_init(bar_mma, 1);
+        s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) tmem_alloc(smem_u32(&s_tmem), TC_TMEM_COLS);
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;  // this warp's TMEM lane quarter
+
+    uint32_t it = 0;         // K/V tiles consumed by this CTA (stage = it % NST)
+    uint32_t mma_phase = 0;  // completions of bar_mma so far (parity)
+    const int nunits = ws.hdr[HDR_NTC];
+    const int64_t nwork = (int64_t)nunits * Hkv;
+    for (;;) {
+        if (tid == 0) s_work = atomicAdd(&ws.hdr[HDR_TC_NEXT], 1);
+        __syncthreads();
+        const int w = s_work;
+        if (w >= nwork || s_abort) break;
+        const int u = w / Hkv, head = w % Hkv;
+        const int32_t* U = ws.units_tc + (int64_t)u * UNIT_INTS;
+        const int q_lo = U[0], q_hi = U[1], t0u = U[2], t1u = U[3], ord = U[4];
+        const int R = (q_hi - q_lo + 1) * G;
+        const int nrt = (R + 127) / 128;
+        const int32_t* tab = table_row(c, layer, slots[q_lo]);
+        const int blk0 = t0u / 16, blk_end = (t1u + 15) / 16;
+        const int ntiles = (blk_end - blk0 + 3) / 4;
+
+        // Q rows -> smem (K-major, swizzled); rows R..nrt*128 zero
+        for (int idx = tid; idx < nrt * 128 * (D / 8); idx += TC_THREADS) {
+            const int r = idx / (D / 8), ch = idx % (D / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < R) {
+                const int seq = q_lo + r / G, g = r % G;
+                v = *reinterpret_cast<const uint4*>(q + (int64_t)seq * q_stride + (int64_t)(head * G + g) * D + ch * 8);
+            }
+            const int rt = r >> 7, rr = r & 127, half = ch >> 3;
+            *reinterpret_cast<uint4*>(smem + TC_OFF_Q + (rt * 2 + half) * 16384 + sw128_off(rr, ch & 7)) = v;
+        }
+        fence_proxy_async();
+        __syncthreads();
+
+        auto issue_tile = [&](int i, uint32_t stage) {
+            const int nb = min(4, blk_end - (blk0 + 4 * i));
+            const uint32_t bar = bar_full0 + 8 * stage;
+            mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2 * 2048));
+            for (int b = 0; b < nb; ++b) {
+                const int blk = tab[blk0 + 4 * i + b];
+                for (int h2 = 0; h2 < HALVES; ++h2) {
+                    const uint32_t off = stage * TC_KV_STAGE + h2 * (TC_TILE * 128) + b * 2048;
+                    tma_load_3d(sbase + TC_OFF_K + off, &tmap_k, bar, h2 * 64, head, blk * 16);
+                    tma_load_3d(sbase + TC_OFF_V + off, &tmap_v, bar, h2 * 64, head, blk * 16);
+                }
+            }
+        };
+        if (tid == 0)
+            for (int i = 0; i < min(TC_NST, ntiles); ++i) issue_tile(i, (it + i) % TC_NST);
+
+        float m_ref[TC_RT], l_sum[TC_RT];
+#pragma unroll
+        for (int rt = 0; rt < TC_RT; ++rt) {
+            m_ref[rt] = -INFINITY;
+            l_sum[rt] = 0.f;
+        }
+        bool ok = true;
+        for (int i = 0; i < ntiles && ok; ++i) {
+            const uint32_t stage = it % TC_NST, kv_phase = (it / TC_NST) & 1;
+            // S = Q K^T
+            if (tid == 0) {
+                if (!mbar_wait(bar_full0 + 8 * stage, kv_phase)) {
+                    s_abort = 1;
+                } else {
+                    tc_fence_after();
+                    for (int rt = 0; rt < nrt; ++rt)
+                        for (int ks = 0; ks < D / 16; ++ks) {
+                            const uint32_t qa = sbase + TC_OFF_Q + (rt * 2 + (ks >> 2)) * 16384 + (ks & 3) * 32;
+                            const uint32_t kb = sbase + TC_OFF_K + stage * TC_KV_STAGE + (ks >> 2) * (TC_TILE * 128) +
+                                                (ks & 3) * 32;
+                            umma_f16(tmem + 256 + rt * 64, sdesc_sw128(qa, 16, 1024), sdesc_sw128(kb, 16, 1024),
+                                     IDESC_QK, ks > 0);
+                        }
+                    umma_commit(bar_mma);
+                }
+            }
+            if (!mbar_wait(bar_mma, mma_phase & 1)) s_abort = 1;
+            ++mma_phase;
+            __syncthreads();
+            if (s_abort) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            // softmax rows (thread = row = TMEM lane)
+            const int tb = (blk0 + 4 * i) * 16;  // first token of the tile
+            for (int rt = 0; rt < nrt; ++rt) {
+                if (rt * 128 + warp * 32 >= R) continue;  // whole warp idle (warp-uniform)
+                const int row = rt * 128 + tid;
+                float sv[TC_TILE];
+                tmem_ld32(tmem + lane_off + 256 + rt * 64, sv);
+                tmem_ld32(tmem + lane_off + 256 + rt * 64 + 32, sv + 32);
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < TC_TILE; ++j) {
+                    const int t = tb + j;
+                    sv[j] = (t >= t0u && t < t1u) ? sv[j] * scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, sv[j]);
+                }
+                const float m_new = fmaxf(m_ref[rt], mx);
+                const bool raise = (m_ref[rt] == -INFINITY) || (m_new > m_ref[rt] + 8.f);
+                // rescale O (warp-collective TMEM access) when any row of the warp raises its reference
+                if (i > 0 && __any_sync(0xffffffffu, raise && row < R)) {
+                    const float f = (raise && row < R) ? exp2f(m_ref[rt] - m_new) : 1.f;
+#pragma unroll
+                    for (int cb = 0; cb < D / 32; ++cb) {
+                        float ov[32];
+                        tmem_ld32(tmem + lane_off + rt * 128 + cb * 32, ov);
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) ov[k] *= f;
+                        tmem_st32(tmem + lane_off + rt * 128 + cb * 32, ov);
+                    }
+                }
+                if (raise) {
+                    if (m_ref[rt] != -INFINITY) l_sum[rt] *= exp2f(m_ref[rt] - m_new);
+                    m_ref[rt] = m_new;
+                }
+                if (row < R) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int ch = 0; ch < TC_TILE / 8; ++ch) {
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const T a = Elem<T>::from_f(exp2f(sv[ch * 8 + 2 * e] - m_ref[rt]));
+                            const T b = Elem<T>::from_f(exp2f(sv[ch * 8 + 2 * e + 1] - m_ref[rt]));
+                            acc += Elem<T>::to_f(a) + Elem<T>::to_f(b);
+                            const uint16_t ua = *reinterpret_cast<const uint16_t*>(&a);
+                            const uint16_t ub = *reinterpret_cast<const uint16_t*>(&b);
+                            pk[e] = (uint32_t)ua | ((uint32_t)ub << 16);
+                        }
+                        *reinterpret_cast<uint4*>(smem + TC_OFF_P + rt * 16384 + sw128_off(tid, ch)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    }
+                    l_sum[rt] += acc;
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async();
+            __syncthreads();
+            // O += P V
+            if (tid == 0) {
+                tc_fence_after();
+                for (int rt = 0; rt < nrt; ++rt)
+                    for (int ks = 0; ks < TC_TILE / 16; ++ks) {
+                        const uint32_t pa = sbase + TC_OFF_P + rt * 16384 + ks * 32;
+                        const uint32_t vb = sbase + TC_OFF_V + stage * TC_KV_STAGE + ks * 2048;
+                        umma_f16(tmem + rt * 128, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, TC_TILE * 128, 1024),
+                                 IDESC_PV, (i > 0 || ks > 0));
+                    }
+                umma_commit(bar_mma);
+            }
+            if (!mbar_wait(bar_mma, mma_phase & 1)) s_abort = 1;
+            ++mma_phase;
+            tc_fence_after();
+            // the stage is free: prefetch tile i + NST into it
+            if (tid == 0 && !s_abort && i + TC_NST < ntiles) issue_tile(i + TC_NST, stage);
+            ++it;
+            __syncthreads();
+            if (s_abort) {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) break;
+        // partials: this thread's rows
+        for (int rt = 0; rt < nrt; ++rt) {
+            if (rt * 128 + warp * 32 >= R) continue;
+            const int row = rt * 128 + tid;
+            const int seq = q_lo + row / G, hq = head * G + row % G;
+            const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
+#pragma unroll
+            for (int cb = 0; cb < D / 32; ++cb) {
+                float ov[32];
+                tmem_ld32(tmem + lane_off + rt * 128 + cb * 32, ov);
+                if (row < R) {
+                    float4* dst = reinterpret_cast<float4*>(ws.part_o + pi * D + cb * 32);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) dst[k] = make_float4(ov[4 * k], ov[4 * k + 1], ov[4 * k + 2], ov[4 * k + 3]);
+                }
+            }
+            if (row < R) {
+                ws.part_ml[pi * 2] = m_ref[rt];
+                ws.part_ml[pi * 2 + 1] = l_sum[rt];
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    // teardown: on abort, drain outstanding copies (bounded) before the smem goes away
+    __syncthreads();
+    if (s_abort) {
+        if (tid == 0) {
+            atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
+            for (int st = 0; st < TC_NST; ++st) {
+                const uint32_t k = it + st;
+                (void)mbar_wait(bar_full0 + 8 * (k % TC_NST), (k / TC_NST) & 1);
+            }
+        }
+        __syncthreads();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, TC_TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// host: tensor maps of a layer's K and V pools (cached per pool and layer)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+struct PoolMaps {
+    const void* k_pool;
+    const void* v_pool;
+    int layer, num_blocks, kv_heads, head_dim, dtype, device;
+    CUtensorMap mk, mv;
+};
+
+static bool make_pool_map(CUtensorMap* m, const mentat_kv_cache* c, const void* pool, int layer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const int esz = dtype_bytes(c->dtype);
+    const int64_t layer_bytes = (int64_t)c->num_blocks * c->block_size * c->num_kv_heads * c->head_dim * esz;
+    void* base = (char*)pool + layer * layer_bytes;
+    cuuint64_t dims[3] = {(cuuint64_t)c->head_dim, (cuuint64_t)c->num_kv_heads,
+                          (cuuint64_t)c->num_blocks * c->block_size};
+    cuuint64_t strides[2] = {(cuuint64_t)c->head_dim * esz, (cuuint64_t)c->num_kv_heads * c->head_dim * esz};
+    cuuint32_t box[3] = {64, 1, 16};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt =
+        c->dtype == MENTAT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return fn(m, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static const PoolMaps* pool_maps(const mentat_kv_cache* c, int layer) {
+    constexpr int CAP = 256;
+    static PoolMaps cache[CAP];
+    static int used = 0, next = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int i = 0; i < used; ++i) {
+        const PoolMaps& e = cache[i];
+        if (e.k_pool == c->k_pool && e.v_pool == c->v_pool && e.layer == layer && e.num_blocks == c->num_blocks &&
+            e.kv_heads == c->num_kv_heads && e.head_dim == c->head_dim && e.dtype == c->dtype && e.device == dev)
+            return &e;
+    }
+    PoolMaps e;
+    e.k_pool = c->k_pool;
+    e.v_pool = c->v_pool;
+    e.layer = layer;
+    e.num_blocks = c->num_blocks;
+    e.kv_heads = c->num_kv_heads;
+    e.head_dim = c->head_dim;
+    e.dtype = c->dtype;
+    e.device = dev;
+    if (!make_pool_map(&e.mk, c, c->k_pool, layer) || !make_pool_map(&e.mv, c, c->v_pool, layer)) return nullptr;
+    const int slot = used < CAP ? used++ : (next++ % CAP);
+    cache[slot] = e;
+    return &cache[slot];
+}
+
+// whether the tensor-core kernel supports this cache layout
+static bool tc_supported(const mentat_kv_cache* c) {
+    return (c->dtype == MENTAT_BF16 || c->dtype == MENTAT_F16) && (c->head_dim == 64 || c->head_dim == 128) &&
+           c->block_size == 16 && c->num_kv_heads * c->head_dim * dtype_bytes(c->dtype) % 16 == 0;
+}
+
+}  // namespace mentat
