@@ -3,19 +3,21 @@
 // tensor-core unit queue (segments with >= tc_min_rows query rows: the shared
 // prefixes of a tree).
 //
-// One CTA per SM (persistent, 4 warps, ~193 KB of shared memory).  Per unit and
+// One CTA per SM (persistent; an issuer warp and two softmax warpgroups; ~193 KB
+// of shared memory).  Per unit and
 // kv head:
 //   * Q rows of all sharing sequences (up to 256 = two M=128 row tiles) are
 //     written once to shared memory in the K-major 128-byte-swizzled layout.
 //   * K and V come in 64-token tiles (4 blocks) by TMA from the paged pool,
-//     through a 3-stage mbarrier ring, each (block, head) box read once for
+//     through a 4-stage mbarrier ring, each (block, head) box read once for
 //     every row of the unit.
 //   * S = Q K^T: tcgen05.mma kind::f16, M=128, N=64, K=head_dim, accumulator
 //     in TMEM.  Each thread owns one query row (TMEM lane): scale, mask, online
 //     softmax in base 2 with a lazily raised reference max (O is rescaled in
 //     TMEM only when the row max grows by more than 2^8), P rounded to the
-//     cache dtype and written K-major swizzled to shared memory.
-//   * O += P V: tcgen05.mma, M=128, N=head_dim, K=64 tokens, V read MN-major.
+//     cache dtype and stored back into TMEM over the S columns it came from.
+//   * O += P V: tcgen05.mma with A = P in TMEM, M=128, N=head_dim, K=64
+//     tokens, V read MN-major from shared memory.
 //   * The unnormalised (m, l, o) partial goes to the workspace like the FFMA
 //     units, and k_merge combines both kinds.
 // Every mbarrier wait is bounded by a clock limit; on timeout the CTA records
@@ -28,20 +30,27 @@
 
 namespace mentat {
 
-constexpr int TC_THREADS = 128;
+#ifdef MENTAT_TC_TRACE
+__device__ long long g_tc_trace[4096];
+#define TC_TRACE(k) do { if (blockIdx.x == 0 && (threadIdx.x == TC_SOFTMAX_WARPS * 32 || threadIdx.x == 0) && g_trace_on && (k) < 2048) g_tc_trace[(k) + (threadIdx.x ? 0 : 2048)] = clock64(); } while (0)
+#else
+#define TC_TRACE(k) do { } while (0)
+#endif
+
+constexpr int TC_SOFTMAX_WARPS = 8;        // two warpgroups: one per 128-row tile
+constexpr int TC_THREADS = (TC_SOFTMAX_WARPS + 2) * 32;  // + an MMA issuer warp and a TMA producer warp
 constexpr int TC_TILE = 64;                 // tokens per K/V tile (4 blocks of 16)
-constexpr int TC_NST = 3;                   // K/V pipeline stages
+constexpr int TC_NST = 4;                   // K/V pipeline stages
 constexpr int TC_RT = 2;                    // row tiles (128 rows each)
 constexpr int TC_Q_BYTES = TC_RT * 2 * 128 * 128;          // 64 KB: [rt][half][128 rows][128 B]
 constexpr int TC_KV_STAGE = 2 * TC_TILE * 128;              // 16 KB: [half][64 tok][128 B]
-constexpr int TC_P_BYTES = TC_RT * 128 * 128;               // 32 KB: [rt][128 rows][128 B]
 constexpr int TC_OFF_Q = 0;
 constexpr int TC_OFF_K = TC_OFF_Q + TC_Q_BYTES;
 constexpr int TC_OFF_V = TC_OFF_K + TC_NST * TC_KV_STAGE;
-constexpr int TC_OFF_P = TC_OFF_V + TC_NST * TC_KV_STAGE;
-constexpr int TC_OFF_BAR = TC_OFF_P + TC_P_BYTES;           // mbarriers: full[NST], mma
+constexpr int TC_OFF_BAR = TC_OFF_V + TC_NST * TC_KV_STAGE;  // mbarriers: full[NST], s[2], pv
 constexpr int TC_SMEM = TC_OFF_BAR + 128 + 1024;            // + alignment slack
-constexpr uint32_t TC_TMEM_COLS = 512;      // O[rt] at rt*128, S[rt] at 256 + rt*64
+constexpr uint32_t TC_TMEM_COLS = 512;      // O[rt] at rt*128, S[buf][rt] at 256 + buf*128 + rt*64
+                                            // (P, packed pairs, overwrites the first 32 columns of its S)
 constexpr long long TC_WAIT_CYCLES = 4000000000ll;  // ~2 s at 1.9 GHz
 
 // ---------------------------------------------------------------------------
@@ -84,6 +93,19 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// named barrier 1 over `count` threads that also ORs a flag across them
+__device__ __forceinline__ int bar_sync_or(int count, int flag) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(out)
+        : "r"(flag), "r"(count)
+        : "memory");
+    return (int)out;
+}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
@@ -101,6 +123,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]: A (K-major) packed two 16-bit values per column
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -161,6 +193,28 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
     return (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u + (uint32_t)((chunk ^ (row & 7)) << 4);
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+    __device__ __forceinline__ static uint32_t pack(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+template <> struct Pair<__half> {
+    __device__ __forceinline__ static uint32_t pack(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+
+// Roles: warps 0-3 softmax row tile 0, warps 4-7 softmax row tile 1 (TMEM
+// lane quarter = warp % 4), warp 8 lane 0 issues the MMAs, warp 9 lane 0 the
+// TMA loads.
 template <typename T, int D>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -170,21 +224,32 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     constexpr int FMT = Elem<T>::code == MENTAT_BF16 ? 1 : 0;
     constexpr uint32_t IDESC_QK = idesc_f16(FMT, 128, TC_TILE, 0, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(FMT, 128, D, 0, 1);
+    constexpr int MAX_BLK = CHUNK_TC / 16 + 1;     // blocks a unit can touch
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t s_tmem;
     __shared__ int s_work, s_abort;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    __shared__ int s_blk[MAX_BLK];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool issuer = (warp >= TC_SOFTMAX_WARPS);
+    const bool leader = warp == TC_SOFTMAX_WARPS && lane == 0;        // MMA issue
+    const bool producer = warp == TC_SOFTMAX_WARPS + 1 && lane == 0;  // TMA issue
+    const int my_rt = warp >> 2;                       // softmax warps: row tile
+    const int my_row = (warp & 3) * 32 + lane;         // row within the tile = TMEM lane
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_full0 = sbase + TC_OFF_BAR;
-    const uint32_t bar_mma = sbase + TC_OFF_BAR + 8 * TC_NST;
+    const uint32_t bar_full0 = sbase + TC_OFF_BAR;     // [NST] K/V tile landed
+    const uint32_t bar_s0 = bar_full0 + 8 * TC_NST;    // [2] S buffer written
+    const uint32_t bar_pv = bar_s0 + 16;               // P V done
+    const uint32_t bar_empty0 = bar_pv + 8;            // [NST] stage consumed (its P V done)
     const int Hkv = c.num_kv_heads, G = Hq / Hkv;
 
-    // zero Q / K / V / P once: padded rows and unloaded tokens must be finite
     for (int i = tid; i < TC_OFF_BAR / 16; i += TC_THREADS) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
         for (int st = 0; st < TC_NST; ++st) mbar_init(bar_full0 + 8 * st, 1);
-        mbar_init(bar_mma, 1);
+        mbar_init(bar_s0, 1);
+        mbar_init(bar_s0 + 8, 1);
+        mbar_init(bar_pv, 1);
+        for (int st = 0; st < TC_NST; ++st) mbar_init(bar_empty0 + 8 * st, 1);
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -194,10 +259,13 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;  // this warp's TMEM lane quarter
-
-    uint32_t it = 0;         // K/V tiles consumed by this CTA (stage = it % NST)
-    uint32_t mma_phase = 0;  // completions of bar_mma so far (parity)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lane quarter
+    // TMEM columns: O[rt] at rt*128; S[buf][rt] at 256 + buf*128 + rt*64
+#ifdef MENTAT_TC_TRACE
+    bool g_trace_on = true;
+#endif
+    uint32_t g0 = 0;      // tiles this CTA has processed before the current unit
+    uint32_t issued = 0;  // tiles whose TMA has been issued (producer; global tile index = issue order)
     const int nunits = ws.hdr[HDR_NTC];
     const int64_t nwork = (int64_t)nunits * Hkv;
     for (;;) {
@@ -205,6 +273,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         __syncthreads();
         const int w = s_work;
         if (w >= nwork || s_abort) break;
+        TC_TRACE(0);
         const int u = w / Hkv, head = w % Hkv;
         const int32_t* U = ws.units_tc + (int64_t)u * UNIT_INTS;
         const int q_lo = U[0], q_hi = U[1], t0u = U[2], t1u = U[3], ord = U[4];
@@ -212,9 +281,10 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         const int nrt = (R + 127) / 128;
         const int32_t* tab = table_row(c, layer, slots[q_lo]);
         const int blk0 = t0u / 16, blk_end = (t1u + 15) / 16;
-        const int ntiles = (blk_end - blk0 + 3) / 4;
+        const int nblk = blk_end - blk0;  // <= MAX_BLK
+        const int ntiles = (nblk + 3) / 4;
 
-        // Q rows -> smem (K-major, swizzled); rows R..nrt*128 zero
+        for (int j = tid; j < nblk; j += TC_THREADS) s_blk[j] = tab[blk0 + j];
         for (int idx = tid; idx < nrt * 128 * (D / 8); idx += TC_THREADS) {
             const int r = idx / (D / 8), ch = idx % (D / 8);
             uint4 v = make_uint4(0, 0, 0, 0);
@@ -227,148 +297,164 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         }
         fence_proxy_async();
         __syncthreads();
+        TC_TRACE(1);
 
-        auto issue_tile = [&](int i, uint32_t stage) {
-            const int nb = min(4, blk_end - (blk0 + 4 * i));
+        auto issue_tile = [&](int i) {  // producer: TMA of the unit's tile i into stage (g0 + i) % NST
+            const uint32_t stage = (g0 + i) % TC_NST;
+            const int nb = min(4, nblk - 4 * i);
             const uint32_t bar = bar_full0 + 8 * stage;
             mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2 * 2048));
             for (int b = 0; b < nb; ++b) {
-                const int blk = tab[blk0 + 4 * i + b];
+                const int blk = s_blk[4 * i + b];
                 for (int h2 = 0; h2 < HALVES; ++h2) {
                     const uint32_t off = stage * TC_KV_STAGE + h2 * (TC_TILE * 128) + b * 2048;
                     tma_load_3d(sbase + TC_OFF_K + off, &tmap_k, bar, h2 * 64, head, blk * 16);
                     tma_load_3d(sbase + TC_OFF_V + off, &tmap_v, bar, h2 * 64, head, blk * 16);
                 }
             }
+            ++issued;
         };
-        if (tid == 0)
-            for (int i = 0; i < min(TC_NST, ntiles); ++i) issue_tile(i, (it + i) % TC_NST);
-
-        float m_ref[TC_RT], l_sum[TC_RT];
-#pragma unroll
-        for (int rt = 0; rt < TC_RT; ++rt) {
-            m_ref[rt] = -INFINITY;
-            l_sum[rt] = 0.f;
-        }
-        bool ok = true;
-        for (int i = 0; i < ntiles && ok; ++i) {
-            const uint32_t stage = it % TC_NST, kv_phase = (it / TC_NST) & 1;
-            // S = Q K^T
-            if (tid == 0) {
-                if (!mbar_wait(bar_full0 + 8 * stage, kv_phase)) {
-                    s_abort = 1;
-                } else {
-                    tc_fence_after();
-                    for (int rt = 0; rt < nrt; ++rt)
-                        for (int ks = 0; ks < D / 16; ++ks) {
-                            const uint32_t qa = sbase + TC_OFF_Q + (rt * 2 + (ks >> 2)) * 16384 + (ks & 3) * 32;
-                            const uint32_t kb = sbase + TC_OFF_K + stage * TC_KV_STAGE + (ks >> 2) * (TC_TILE * 128) +
-                                                (ks & 3) * 32;
-                            umma_f16(tmem + 256 + rt * 64, sdesc_sw128(qa, 16, 1024), sdesc_sw128(kb, 16, 1024),
-                                     IDESC_QK, ks > 0);
-                        }
-                    umma_commit(bar_mma);
-                }
+        auto issue_qk = [&](int i) {  // leader: S[(g0+i)%2] = Q K(i)^T once tile i landed
+            const uint32_t g = g0 + i, stage = g % TC_NST;
+            TC_TRACE(1024 + 4 * i);
+            if (!mbar_wait(bar_full0 + 8 * stage, (g / TC_NST) & 1)) {
+                s_abort = 1;
+                return;
             }
-            if (!mbar_wait(bar_mma, mma_phase & 1)) s_abort = 1;
-            ++mma_phase;
-            __syncthreads();
-            if (s_abort) {
-                ok = false;
-                break;
-            }
+            TC_TRACE(1025 + 4 * i);
             tc_fence_after();
-            // softmax rows (thread = row = TMEM lane)
-            const int tb = (blk0 + 4 * i) * 16;  // first token of the tile
-            for (int rt = 0; rt < nrt; ++rt) {
-                if (rt * 128 + warp * 32 >= R) continue;  // whole warp idle (warp-uniform)
-                const int row = rt * 128 + tid;
-                float sv[TC_TILE];
-                tmem_ld32(tmem + lane_off + 256 + rt * 64, sv);
-                tmem_ld32(tmem + lane_off + 256 + rt * 64 + 32, sv + 32);
-                float mx = -INFINITY;
-#pragma unroll
-                for (int j = 0; j < TC_TILE; ++j) {
-                    const int t = tb + j;
-                    sv[j] = (t >= t0u && t < t1u) ? sv[j] * scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, sv[j]);
+            const uint32_t sbuf = 256 + (g & 1) * 128;
+            for (int rt = 0; rt < nrt; ++rt)
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t qa = sbase + TC_OFF_Q + (rt * 2 + (ks >> 2)) * 16384 + (ks & 3) * 32;
+                    const uint32_t kb = sbase + TC_OFF_K + stage * TC_KV_STAGE + (ks >> 2) * (TC_TILE * 128) + (ks & 3) * 32;
+                    umma_f16(tmem + sbuf + rt * 64, sdesc_sw128(qa, 16, 1024), sdesc_sw128(kb, 16, 1024), IDESC_QK,
+                             ks > 0);
                 }
-                const float m_new = fmaxf(m_ref[rt], mx);
-                const bool raise = (m_ref[rt] == -INFINITY) || (m_new > m_ref[rt] + 8.f);
-                // rescale O (warp-collective TMEM access) when any row of the warp raises its reference
-                if (i > 0 && __any_sync(0xffffffffu, raise && row < R)) {
-                    const float f = (raise && row < R) ? exp2f(m_ref[rt] - m_new) : 1.f;
+            umma_commit(bar_s0 + 8 * (g & 1));
+            TC_TRACE(1026 + 4 * i);
+        };
+        if (producer) {
+            // a stage is reused once the P V of the tile that last used it is done
+            for (int i = 0; i < ntiles && !s_abort; ++i) {
+                const uint32_t gi = g0 + i;
+                if (gi >= TC_NST && !mbar_wait(bar_empty0 + 8 * (gi % TC_NST), ((gi / TC_NST) - 1) & 1)) {
+                    s_abort = 1;
+                    break;
+                }
+#ifdef MENTAT_TC_TRACE
+                if (blockIdx.x == 0 && g_trace_on) g_tc_trace[1536 + i] = clock64();
+#endif
+                issue_tile(i);
+            }
+        }
+        if (leader) issue_qk(0);
+
+        float m_ref = -INFINITY, l_sum = 0.f;  // softmax warps: this thread's row
+        const bool wact = !issuer && my_rt < nrt && (my_rt * 128 + (warp & 3) * 32 < R);  // warp-uniform
+        const int row = my_rt * 128 + my_row;
+        int aborted = 0;
+        for (int i = 0; i < ntiles && warp <= TC_SOFTMAX_WARPS; ++i) {
+            const uint32_t g = g0 + i;
+            TC_TRACE(8 + 8 * i);
+            // keep the tensor pipe busy with S(i+1) while tile i's softmax runs
+            if (leader && !s_abort && i + 1 < ntiles) issue_qk(i + 1);
+            TC_TRACE(9 + 8 * i);
+            uint32_t pk[TC_TILE / 2];
+            float fac = 1.f;
+            if (wact) {
+                if (!mbar_wait(bar_s0 + 8 * (g & 1), (g >> 1) & 1)) s_abort = 1;
+                tc_fence_after();
+                TC_TRACE(10 + 8 * i);
+                const int tb = (blk0 + 4 * i) * 16;  // first token of the tile
+                float sv[TC_TILE];
+                tmem_ld32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64, sv);
+                tmem_ld32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64 + 32, sv + 32);
+                float mx = -INFINITY;
+                if (tb >= t0u && tb + TC_TILE <= t1u) {
+#pragma unroll
+                    for (int j = 0; j < TC_TILE; ++j) {
+                        sv[j] *= scale_log2;
+                        mx = fmaxf(mx, sv[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < TC_TILE; ++j) {
+                        const int t = tb + j;
+                        sv[j] = (t >= t0u && t < t1u) ? sv[j] * scale_log2 : -INFINITY;
+                        mx = fmaxf(mx, sv[j]);
+                    }
+                }
+                const float m_new = fmaxf(m_ref, mx);
+                if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
+                    if (m_ref != -INFINITY) {
+                        fac = ex2_approx(m_ref - m_new);
+                        l_sum *= fac;
+                    }
+                    m_ref = m_new;
+                }
+                float acc = 0.f;
+#pragma unroll
+                for (int e = 0; e < TC_TILE / 2; ++e) {
+                    const float a = ex2_approx(sv[2 * e] - m_ref), b = ex2_approx(sv[2 * e + 1] - m_ref);
+                    acc += a + b;
+                    pk[e] = Pair<T>::pack(a, b);
+                }
+                l_sum += acc;
+                TC_TRACE(11 + 8 * i);
+                // P over the consumed S columns; P V(i-1) read the other S buffer, so no wait is needed
+                tmem_st32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64, reinterpret_cast<const float*>(pk));
+                TC_TRACE(12 + 8 * i);
+                // rows whose reference max rose rescale O, after P V(i-1) is done
+                if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
+                    if (!mbar_wait(bar_pv, (g - 1) & 1)) s_abort = 1;
+                    tc_fence_after();
+                    const float f = row < R ? fac : 1.f;
 #pragma unroll
                     for (int cb = 0; cb < D / 32; ++cb) {
                         float ov[32];
-                        tmem_ld32(tmem + lane_off + rt * 128 + cb * 32, ov);
+                        tmem_ld32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
 #pragma unroll
                         for (int k = 0; k < 32; ++k) ov[k] *= f;
-                        tmem_st32(tmem + lane_off + rt * 128 + cb * 32, ov);
+                        tmem_st32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
                     }
                 }
-                if (raise) {
-                    if (m_ref[rt] != -INFINITY) l_sum[rt] *= exp2f(m_ref[rt] - m_new);
-                    m_ref[rt] = m_new;
-                }
-                if (row < R) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int ch = 0; ch < TC_TILE / 8; ++ch) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const T a = Elem<T>::from_f(exp2f(sv[ch * 8 + 2 * e] - m_ref[rt]));
-                            const T b = Elem<T>::from_f(exp2f(sv[ch * 8 + 2 * e + 1] - m_ref[rt]));
-                            acc += Elem<T>::to_f(a) + Elem<T>::to_f(b);
-                            const uint16_t ua = *reinterpret_cast<const uint16_t*>(&a);
-                            const uint16_t ub = *reinterpret_cast<const uint16_t*>(&b);
-                            pk[e] = (uint32_t)ua | ((uint32_t)ub << 16);
-                        }
-                        *reinterpret_cast<uint4*>(smem + TC_OFF_P + rt * 16384 + sw128_off(tid, ch)) =
-                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                    l_sum[rt] += acc;
-                }
+                TC_TRACE(13 + 8 * i);
             }
             tc_fence_before();
-            fence_proxy_async();
-            __syncthreads();
-            // O += P V
-            if (tid == 0) {
+            aborted = bar_sync_or(TC_SOFTMAX_WARPS * 32 + 32, s_abort);  // P(i) stored (softmax warps + issuer)
+            TC_TRACE(14 + 8 * i);
+            if (aborted) break;
+            if (leader) {  // O += P V(i)
                 tc_fence_after();
+                const uint32_t stage = g % TC_NST;
                 for (int rt = 0; rt < nrt; ++rt)
                     for (int ks = 0; ks < TC_TILE / 16; ++ks) {
-                        const uint32_t pa = sbase + TC_OFF_P + rt * 16384 + ks * 32;
+                        const uint32_t pa = tmem + 256 + (g & 1) * 128 + rt * 64 + ks * 8;
                         const uint32_t vb = sbase + TC_OFF_V + stage * TC_KV_STAGE + ks * 2048;
-                        umma_f16(tmem + rt * 128, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, TC_TILE * 128, 1024),
-                                 IDESC_PV, (i > 0 || ks > 0));
+                        umma_f16_ts(tmem + rt * 128, pa, sdesc_sw128(vb, TC_TILE * 128, 1024), IDESC_PV,
+                                    (i > 0 || ks > 0));
                     }
-                umma_commit(bar_mma);
+                umma_commit(bar_pv);
+                umma_commit(bar_empty0 + 8 * stage);
             }
-            if (!mbar_wait(bar_mma, mma_phase & 1)) s_abort = 1;
-            ++mma_phase;
-            tc_fence_after();
-            // the stage is free: prefetch tile i + NST into it
-            if (tid == 0 && !s_abort && i + TC_NST < ntiles) issue_tile(i + TC_NST, stage);
-            ++it;
-            __syncthreads();
-            if (s_abort) {
-                ok = false;
-                break;
-            }
+            TC_TRACE(15 + 8 * i);
         }
-        if (!ok) break;
-        // partials: this thread's rows
-        for (int rt = 0; rt < nrt; ++rt) {
-            if (rt * 128 + warp * 32 >= R) continue;
-            const int row = rt * 128 + tid;
+        // every thread reaches this CTA-wide barrier, so the abort decision is uniform
+        if (__syncthreads_or(aborted || s_abort)) {
+            s_abort = 1;
+            break;
+        }
+        // last P V done -> partials of this thread's row
+        if (wact) {
+            if (!mbar_wait(bar_pv, (g0 + ntiles - 1) & 1)) s_abort = 1;
+            tc_fence_after();
             const int seq = q_lo + row / G, hq = head * G + row % G;
             const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
 #pragma unroll
             for (int cb = 0; cb < D / 32; ++cb) {
                 float ov[32];
-                tmem_ld32(tmem + lane_off + rt * 128 + cb * 32, ov);
+                tmem_ld32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
                 if (row < R) {
                     float4* dst = reinterpret_cast<float4*>(ws.part_o + pi * D + cb * 32);
 #pragma unroll
@@ -376,23 +462,29 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 }
             }
             if (row < R) {
-                ws.part_ml[pi * 2] = m_ref[rt];
-                ws.part_ml[pi * 2 + 1] = l_sum[rt];
+                ws.part_ml[pi * 2] = m_ref;
+                ws.part_ml[pi * 2 + 1] = l_sum;
             }
+        } else if (leader) {
+            if (!mbar_wait(bar_pv, (g0 + ntiles - 1) & 1)) s_abort = 1;  // keep the phase count of every waiter in step
         }
+        TC_TRACE(4);
+#ifdef MENTAT_TC_TRACE
+        g_trace_on = false;
+#endif
+        g0 += ntiles;
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
     }
-    // teardown: on abort, drain outstanding copies (bounded) before the smem goes away
+    // teardown: on abort, drain the copies still in flight (bounded) before the smem goes away
     __syncthreads();
     if (s_abort) {
-        if (tid == 0) {
-            atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
-            for (int st = 0; st < TC_NST; ++st) {
-                const uint32_t k = it + st;
+        if (leader) atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
+        if (producer) {
+            // at most NST tiles can be issued and not yet waited for
+            for (uint32_t k = issued > TC_NST ? issued - TC_NST : 0; k < issued; ++k)
                 (void)mbar_wait(bar_full0 + 8 * (k % TC_NST), (k / TC_NST) & 1);
-            }
         }
         __syncthreads();
     }

@@ -158,9 +158,11 @@ class PagedKVCacheManager:
         self.strict = strict
         self.max_seqs = max_seqs
         self.max_blocks_per_seq = min(max_blocks, max_blocks_per_seq or max_blocks)
+        # table row stride: a multiple of 4 entries keeps every row 16-byte aligned for vector loads
+        self._table_stride = (self.max_blocks_per_seq + 3) // 4 * 4
         self._lib = _lib.load()
 
-        dev, L, mbps = self.device, num_layers, self.max_blocks_per_seq
+        dev, L, mbps = self.device, num_layers, self._table_stride
         shape = (L, max_blocks, block_size, num_key_value_heads, head_dim)
         self._k_all = torch.zeros(shape, device=dev, dtype=dtype)
         self._v_all = torch.zeros(shape, device=dev, dtype=dtype)
