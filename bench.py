@@ -237,7 +237,7 @@ def run_mentat(args):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    stage = (ctypes.c_double * 4)()
+    stage = (ctypes.c_double * 5)()
     cnt = ctypes.c_int32()
     _lib.check(lib.mentat_profile_collect(stage, ctypes.byref(cnt)), "mentat_profile_collect")
     lib.mentat_profile_enable(0)
@@ -285,19 +285,22 @@ def run_mentat(args):
     e2e_val = e2e_all / (e2e_max / 1e3) / 1e9
     n_prof = max(cnt.value, 1)
     st_ms = {"plan": stage[0] / n_prof, "units_ffma": stage[1] / n_prof, "units_tc": stage[2] / n_prof,
-             "merge": stage[3] / n_prof}
-    # bytes each unit kernel streams: the shared prefix goes to the tensor-core units
-    # (64 branches x 4 query heads >= 16 rows), the branch suffixes to the FFMA units
+             "units_tcn": stage[3] / n_prof, "merge": stage[4] / n_prof}
+    # bytes each unit kernel streams: the shared prefix (64 branches x 4 query heads = 256 rows) goes
+    # to the wide tensor-core units, the branch suffixes (4 rows) to the narrow ones (or to the
+    # FFMA units when MENTAT_TC_MIN_ROWS routes them there)
     shared_b = unique_bytes(PREFIX, [0])
-    dom = "units_tc" if st_ms["units_tc"] >= st_ms["units_ffma"] else "units_ffma"
-    dom_bytes = shared_b if dom == "units_tc" else ub - shared_b
+    suffix_kernel = "units_tcn" if st_ms["units_tcn"] >= st_ms["units_ffma"] else "units_ffma"
+    per = {"units_tc": shared_b, suffix_kernel: ub - shared_b}
+    dom = max(per, key=lambda k: st_ms[k])
+    dom_bytes = per[dom]
     units_ms = st_ms[dom]
 
     if rank == 0:
         peak, peak_kind = peaks()
         achieved = dom_bytes / (units_ms / 1e3) / 1e9 if units_ms > 0 else None
-        kernels = {"k_units_tc": {"bytes": shared_b, "ms": st_ms["units_tc"]},
-                   "k_units (FFMA)": {"bytes": ub - shared_b, "ms": st_ms["units_ffma"]}}
+        kernels = {{"units_tc": "k_units_tc", "units_tcn": "k_units_tcn", "units_ffma": "k_units"}[k]:
+                   {"bytes": b, "ms": st_ms[k]} for k, b in per.items()}
         for kv in kernels.values():
             kv["GBps"] = round(kv["bytes"] / (kv["ms"] / 1e3) / 1e9, 1) if kv["ms"] > 0 else None
         cpu = None
@@ -314,7 +317,8 @@ def run_mentat(args):
                        "unique_kv_bytes_per_step_per_rank": ub, "global_batch": NBR * world,
                        "parallelism": f"independent trees x{world}",
                        "l2": "inputs larger than L2 (unique KV > 126 MB), no flush"},
-            "roofline": {"bound": "hbm", "kernel": {"units_tc": "k_units_tc", "units_ffma": "k_units"}[dom],
+            "roofline": {"bound": "hbm",
+                         "kernel": {"units_tc": "k_units_tc", "units_tcn": "k_units_tcn", "units_ffma": "k_units"}[dom],
                          "achieved": round(achieved, 2) if achieved else None, "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
                          "traffic": ncu_traffic().get(f"{dom}_c4_bytes_per_launch"),
@@ -327,7 +331,7 @@ def run_mentat(args):
                     "d2h_bytes_per_step": int(out_host.numel() * 2),
                     "path": "pinned H2D q + new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
                             "D2H output"},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 6 * args.steps,  # lcp, plan, FFMA units, wide + narrow tensor-core units, merge
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

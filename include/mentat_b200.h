@@ -170,9 +170,10 @@ int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t layer, const i
 /* Stage timing of mentat_paged_decode with CUDA events recorded on the launch
  * stream, for up to max_records launches (0 disables).  No counterpart in the
  * reference; used by the benchmark's roofline report.  collect waits for the
- * last recorded launch and returns, in stage_ms[4], the summed milliseconds of
- * the plan, the FFMA units, the tensor-core units and the merge, plus the
- * number of launches, and restarts the record. */
+ * last recorded launch and returns, in stage_ms[5], the summed milliseconds of
+ * the plan (with the table compare), the FFMA units, the wide and the narrow
+ * tensor-core units and the merge, plus the number of launches, and restarts
+ * the record. */
 int mentat_profile_enable(int32_t max_records);
 int mentat_profile_collect(double* stage_ms, int32_t* launches);
 

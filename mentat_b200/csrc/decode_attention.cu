@@ -32,12 +32,15 @@ __device__ long long g_plan_trace[16];
 namespace mentat {
 
 constexpr int PLAN_HDR = 64;        // header ints, see HDR_*
-constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC_NEXT = 4, HDR_TC_ABORT = 5;
+constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC_NEXT = 4, HDR_TC_ABORT = 5,
+              HDR_NTCN = 6, HDR_TCN_NEXT = 7;
+constexpr int KIND_FFMA = 0, KIND_TC = 1, KIND_TCN = 2, NKINDS = 3;
 constexpr int UNIT_INTS = 8;        // seq_lo, seq_hi, tok0, tok1, ordinal
 constexpr int CHUNK = 256;          // tokens per FFMA unit
 constexpr int CHUNK_TC = 2048;      // tokens per tensor-core unit
 constexpr int MAX_ROWS = 16;        // query rows per unit on the FFMA path
-constexpr int TC_MAX_ROWS = 256;    // query rows per unit on the tensor-core path (two M=128 tiles)
+constexpr int TC_MAX_ROWS = 256;    // query rows per unit on the wide tensor-core path (two M=128 tiles)
+constexpr int TCN_MAX_ROWS = 32;    // query rows per unit on the narrow (transposed) tensor-core path
 constexpr int PLAN_MAX_SEQS = 512;  // sequences per launch (callers split larger batches)
 
 struct DecodeWs {
@@ -45,7 +48,8 @@ struct DecodeWs {
     int32_t* nparts;  // [n]
     int32_t* lcp;     // [n] first differing block of pair (i-1, i), filled by k_lcp
     int32_t* units;   // [n * max_parts][UNIT_INTS]  FFMA units
-    int32_t* units_tc;  // [n * max_parts][UNIT_INTS]  tensor-core units
+    int32_t* units_tc;  // [n * max_parts][UNIT_INTS]  wide tensor-core units
+    int32_t* units_tcn; // [n * max_parts][UNIT_INTS]  narrow tensor-core units
     float* part_ml;   // [n][max_parts][Hq][2]
     float* part_o;    // [n][max_parts][Hq][D]
 };
@@ -66,6 +70,7 @@ __host__ __device__ inline void ws_carve(void* base, int n, int hq, int d, int m
     w->lcp = reinterpret_cast<int32_t*>(take((int64_t)n * 4));
     w->units = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
     w->units_tc = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
+    w->units_tcn = reinterpret_cast<int32_t*>(take((int64_t)n * max_parts * UNIT_INTS * 4));
     w->part_ml = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * 2 * 4));
     w->part_o = reinterpret_cast<float*>(take((int64_t)n * max_parts * hq * d * 4));
     *total = off;
@@ -132,21 +137,27 @@ __global__ void __launch_bounds__(LCP_THREADS) k_lcp(mentat_kv_cache c, int laye
 }
 
 // Plan parameters for one launch.  A segment (node of the LCP-interval tree or
-// a sequence's own leaf range) with rows = width x G goes to the tensor-core
-// unit kernel when tc_min_rows <= rows (and the layout supports it), else to
-// the FFMA kernel.
+// a sequence's own leaf range) with rows = width x G goes to
+//   the narrow tensor-core kernel when narrow_ok and rows <= 32,
+//   the wide tensor-core kernel when tc_ok and rows >= tc_min_rows,
+//   the FFMA kernel otherwise.
 struct PlanParams {
     int G;
-    int tc_ok;        // dtype / head_dim / block size fit the tensor-core kernel
-    int tc_min_rows;  // rows threshold for the tensor-core kernel
+    int tc_ok;        // dtype / head_dim / block size fit the wide tensor-core kernel
+    int narrow_ok;    // ... and the narrow one
+    int tc_min_rows;  // rows threshold for the tensor-core kernels
 };
 
-__device__ __forceinline__ bool seg_is_tc(const PlanParams& pp, int width) {
-    return pp.tc_ok && width * pp.G >= pp.tc_min_rows;
+__device__ __forceinline__ int seg_kind(const PlanParams& pp, int width) {
+    const int rows = width * pp.G;
+    if (!pp.tc_ok || rows < pp.tc_min_rows) return KIND_FFMA;
+    if (pp.narrow_ok && rows <= TCN_MAX_ROWS) return KIND_TCN;
+    return KIND_TC;
 }
-__device__ __forceinline__ int seg_chunk(bool tc) { return tc ? CHUNK_TC : CHUNK; }
-__device__ __forceinline__ int seg_spu(const PlanParams& pp, bool tc) {
-    return max(1, (tc ? TC_MAX_ROWS : MAX_ROWS) / pp.G);
+__device__ __forceinline__ int seg_chunk(int kind) { return kind == KIND_FFMA ? CHUNK : CHUNK_TC; }
+__device__ __forceinline__ int seg_spu(const PlanParams& pp, int kind) {
+    const int rows = kind == KIND_FFMA ? MAX_ROWS : (kind == KIND_TC ? TC_MAX_ROWS : TCN_MAX_ROWS);
+    return max(1, rows / pp.G);
 }
 
 __global__ void __launch_bounds__(1024)
@@ -159,8 +170,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __shared__ int s_post[PLAN_MAX_SEQS];     // node ids in pop (post) order
     __shared__ int s_nbase[PLAN_MAX_SEQS], s_nchunk[PLAN_MAX_SEQS];
     __shared__ int s_seg_units[2 * PLAN_MAX_SEQS];  // internal nodes, then leaves
-    __shared__ int s_seg_first[2 * PLAN_MAX_SEQS];  // first FFMA unit of each segment
-    __shared__ int s_seg_first_tc[2 * PLAN_MAX_SEQS];  // first tensor-core unit of each segment
+    __shared__ int s_seg_first[NKINDS][2 * PLAN_MAX_SEQS];  // first unit of each segment in its kind's queue
     __shared__ int smem32[32];
     __shared__ int s_nnodes, s_err;
     const int tid = threadIdx.x;
@@ -223,7 +233,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
             const int x = s_post[k];
             const int p = s_npar[x];
             const int pdep = p >= 0 ? s_ndep[p] : 0;
-            const int ch = seg_chunk(seg_is_tc(pp, s_nhi[x] - s_nlo[x] + 1));
+            const int ch = seg_chunk(seg_kind(pp, s_nhi[x] - s_nlo[x] + 1));
             s_nchunk[x] = (s_ndep[x] - pdep + ch - 1) / ch;
             s_nbase[x] = p >= 0 ? s_nbase[p] + s_nchunk[p] : 0;
         }
@@ -232,12 +242,12 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     PLAN_TRACE(3);
     const int nn = s_nnodes;
     const int nseg = nn + n;
-    const bool leaf_tc = seg_is_tc(pp, 1);
+    const int leaf_kind = seg_kind(pp, 1);
     for (int s = tid; s < nseg; s += blockDim.x) {
         int cnt;
         if (s < nn) {
             const int width = s_nhi[s] - s_nlo[s] + 1;
-            const int spu = seg_spu(pp, seg_is_tc(pp, width));
+            const int spu = seg_spu(pp, seg_kind(pp, width));
             cnt = s_nchunk[s] * ((width + spu - 1) / spu);
         } else {
             const int i = s - nn;
@@ -246,7 +256,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
             const int node = da >= db ? a : b;
             const int d0 = node >= 0 ? s_ndep[node] : 0;
             const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
-            const int chunk = seg_chunk(leaf_tc);
+            const int chunk = seg_chunk(leaf_kind);
             const int ch = (s_len[i] - d0 + chunk - 1) / chunk;
             cnt = ch;
             ws.nparts[i] = base + ch;
@@ -258,38 +268,35 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     PLAN_TRACE(4);
     // exclusive scans of the unit counts, separately per kernel kind
     const int s0 = 2 * tid, s1 = 2 * tid + 1;
-    auto is_tc_seg = [&](int s) { return s < nn ? seg_is_tc(pp, s_nhi[s] - s_nlo[s] + 1) : leaf_tc; };
-    int total_simt, total_tc;
-    {
-        const int c0 = (s0 < nseg && !is_tc_seg(s0)) ? s_seg_units[s0] : 0;
-        const int c1 = (s1 < nseg && !is_tc_seg(s1)) ? s_seg_units[s1] : 0;
-        const int e = block_exclusive_scan(c0 + c1, &total_simt, smem32);
-        if (s0 < nseg) s_seg_first[s0] = e;
-        if (s1 < nseg) s_seg_first[s1] = e + c0;
-    }
-    {
-        const int c0 = (s0 < nseg && is_tc_seg(s0)) ? s_seg_units[s0] : 0;
-        const int c1 = (s1 < nseg && is_tc_seg(s1)) ? s_seg_units[s1] : 0;
-        const int e = block_exclusive_scan(c0 + c1, &total_tc, smem32);
-        if (s0 < nseg) s_seg_first_tc[s0] = e;
-        if (s1 < nseg) s_seg_first_tc[s1] = e + c0;
+    auto kind_of = [&](int s) { return s < nn ? seg_kind(pp, s_nhi[s] - s_nlo[s] + 1) : leaf_kind; };
+    int totals[NKINDS];
+#pragma unroll
+    for (int kind = 0; kind < NKINDS; ++kind) {
+        const int c0 = (s0 < nseg && kind_of(s0) == kind) ? s_seg_units[s0] : 0;
+        const int c1 = (s1 < nseg && kind_of(s1) == kind) ? s_seg_units[s1] : 0;
+        const int e = block_exclusive_scan(c0 + c1, &totals[kind], smem32);
+        if (s0 < nseg) s_seg_first[kind][s0] = e;
+        if (s1 < nseg) s_seg_first[kind][s1] = e + c0;
     }
     if (tid == 0) {
-        if ((int64_t)total_simt > (int64_t)n * max_parts || (int64_t)total_tc > (int64_t)n * max_parts) s_err = 1;
-        ws.hdr[HDR_NSIMT] = s_err ? 0 : total_simt;
+        for (int kind = 0; kind < NKINDS; ++kind)
+            if ((int64_t)totals[kind] > (int64_t)n * max_parts) s_err = 1;
+        ws.hdr[HDR_NSIMT] = s_err ? 0 : totals[KIND_FFMA];
         ws.hdr[HDR_SIMT_NEXT] = 0;
         ws.hdr[HDR_ERR] = s_err;
-        ws.hdr[HDR_NTC] = s_err ? 0 : total_tc;
+        ws.hdr[HDR_NTC] = s_err ? 0 : totals[KIND_TC];
         ws.hdr[HDR_TC_NEXT] = 0;
-        if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, total_simt + total_tc);
+        ws.hdr[HDR_NTCN] = s_err ? 0 : totals[KIND_TCN];
+        ws.hdr[HDR_TCN_NEXT] = 0;
+        if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, totals[0] + totals[1] + totals[2]);
     }
     __syncthreads();
     PLAN_TRACE(5);
     if (s_err) return;
-    for (int kind = 0; kind < 2; ++kind) {
-        const int total = kind ? total_tc : total_simt;
-        const int* first = kind ? s_seg_first_tc : s_seg_first;
-        int32_t* units = kind ? ws.units_tc : ws.units;
+    for (int kind = 0; kind < NKINDS; ++kind) {
+        const int total = totals[kind];
+        const int* first = s_seg_first[kind];
+        int32_t* units = kind == KIND_FFMA ? ws.units : (kind == KIND_TC ? ws.units_tc : ws.units_tcn);
         for (int u = tid; u < total; u += blockDim.x) {
             int lo = 0, hi = nseg - 1;  // last segment whose first unit <= u (zero-count segments precede it)
             while (lo < hi) {
@@ -300,8 +307,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
             int q_lo, q_hi, t0, t1, ord;
             if (s < nn) {
                 const int width = s_nhi[s] - s_nlo[s] + 1;
-                const bool tc = seg_is_tc(pp, width);
-                const int spu = seg_spu(pp, tc), chunk = seg_chunk(tc);
+                const int sk = seg_kind(pp, width);
+                const int spu = seg_spu(pp, sk), chunk = seg_chunk(sk);
                 const int ngroups = (width + spu - 1) / spu;
                 const int ch = k / ngroups, rg = k % ngroups;
                 const int p = s_npar[s];
@@ -318,7 +325,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
                 const int node = da >= db ? a : b;
                 const int d0 = node >= 0 ? s_ndep[node] : 0;
                 const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
-                const int chunk = seg_chunk(leaf_tc);
+                const int chunk = seg_chunk(leaf_kind);
                 q_lo = q_hi = i;
                 t0 = d0 + k * chunk;
                 t1 = min(s_len[i], t0 + chunk);
@@ -530,12 +537,14 @@ __global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts,
 }  // namespace mentat
 
 #include "decode_tc.cuh"
+#include "decode_tcn.cuh"
 
 namespace mentat {
 
-// optional per-launch stage timing (plan, FFMA units, tensor-core units,
-// merge) with CUDA events on the launch stream; enabled by mentat_profile_enable
-constexpr int PROF_STAGES = 4;
+// optional per-launch stage timing (plan, FFMA units, wide tensor-core units,
+// narrow tensor-core units, merge) with CUDA events on the launch stream;
+// enabled by mentat_profile_enable
+constexpr int PROF_STAGES = 5;
 constexpr int PROF_MAX = 4096;
 static cudaEvent_t g_prof_ev[PROF_STAGES + 1][PROF_MAX];
 static int g_prof_cap = 0, g_prof_n = 0;
@@ -570,28 +579,42 @@ static int tc_min_rows() {
     return v;
 }
 
+// narrow (transposed) tensor-core units for segments of <= 32 rows; on by
+// default, MENTAT_NARROW=0 sends those segments to the wide kernel instead
+static bool narrow_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MENTAT_NARROW");
+        v = (e && *e) ? (atoi(e) != 0) : 1;
+    }
+    return v != 0;
+}
+
 template <typename T, int D>
 static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,
                          int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
                          int max_parts, cudaStream_t s) {
     const int G = Hq / c->num_kv_heads;
     const PoolMaps* maps = nullptr;
-    bool tc_ok = false;
+    bool tc_ok = false, narrow_ok = false;
     if constexpr (!std::is_same<T, float>::value) {
         tc_ok = tc_supported(c) && tc_min_rows() <= TC_MAX_ROWS && ((uintptr_t)q % 16 == 0) && (q_stride % 8 == 0);
         if (tc_ok) {
             maps = pool_maps(c, layer);
             tc_ok = maps != nullptr;
         }
+        narrow_ok = tc_ok && D == 128 && narrow_enabled();
         static bool attr = false;
         if (tc_ok && !attr) {
             if (cudaFuncSetAttribute(k_units_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
-                cudaSuccess)
+                    cudaSuccess ||
+                cudaFuncSetAttribute(k_units_tcn<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TCN_SMEM) !=
+                    cudaSuccess)
                 return MENTAT_ERR_CUDA;
             attr = true;
         }
     }
-    PlanParams pp{G, tc_ok ? 1 : 0, tc_min_rows()};
+    PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows()};
     prof_mark(0, s);
     if (n > 1) {
         if (cudaMemsetAsync(ws.lcp, 0x7F, sizeof(int32_t) * n, s) != cudaSuccess) return MENTAT_ERR_CUDA;
@@ -616,10 +639,19 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
         }
     }
     prof_mark(3, s);
+    if constexpr (!std::is_same<T, float>::value && D == 128) {
+        if (narrow_ok) {
+            k_units_tcn<T, D><<<num_sms(), TCN_THREADS, TCN_SMEM, s>>>(maps->mk, maps->mv, *c, layer, slots,
+                                                                       reinterpret_cast<const T*>(q), q_stride, Hq,
+                                                                       qscale, ws, max_parts);
+            MENTAT_CHECK_LAUNCH();
+        }
+    }
+    prof_mark(4, s);
     dim3 mg(n, Hq);
     k_merge<T, D><<<mg, D, 0, s>>>(Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride);
     MENTAT_CHECK_LAUNCH();
-    prof_mark(4, s);
+    prof_mark(5, s);
     if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;
     return MENTAT_OK;
 }
