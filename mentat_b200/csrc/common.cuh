@@ -67,6 +67,34 @@ __device__ __forceinline__ bool has_error(const mentat_kv_cache& c) {
 // ---------------------------------------------------------------------------
 // block-wide exclusive scan of ints (blockDim.x a multiple of 32, <= 1024)
 // ---------------------------------------------------------------------------
+// 64-bit variant (several small counters packed in one word)
+__device__ __forceinline__ long long block_exclusive_scan64(long long v, long long* total, long long* smem32) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+    long long x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        long long y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) smem32[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        long long w = lane < nwarps ? smem32[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            long long y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        smem32[lane] = w;
+    }
+    __syncthreads();
+    long long base = warp ? smem32[warp - 1] : 0;
+    *total = smem32[nwarps - 1];
+    __syncthreads();
+    return base + x - v;
+}
+
 __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* smem32) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nwarps = (blockDim.x + 31) >> 5;

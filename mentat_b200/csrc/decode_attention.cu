@@ -148,6 +148,8 @@ struct PlanParams {
     int tc_min_rows;  // rows threshold for the tensor-core kernels
 };
 
+constexpr int LPT_BUCKETS = CHUNK_TC / 128;  // tensor-core units by 128-token tile count
+
 __device__ __forceinline__ int seg_kind(const PlanParams& pp, int width) {
     const int rows = width * pp.G;
     if (!pp.tc_ok || rows < pp.tc_min_rows) return KIND_FFMA;
@@ -167,11 +169,15 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __shared__ int s_h[PLAN_MAX_SEQS + 1];    // h[i] = LCP(i-1, i) in tokens, h[0] = h[n] = 0
     __shared__ int s_top[PLAN_MAX_SEQS + 1];  // deepest node covering i-1, i after boundary i
     __shared__ int s_nlo[PLAN_MAX_SEQS], s_nhi[PLAN_MAX_SEQS], s_ndep[PLAN_MAX_SEQS], s_npar[PLAN_MAX_SEQS];
-    __shared__ int s_post[PLAN_MAX_SEQS];     // node ids in pop (post) order
+    __shared__ int s_nid[PLAN_MAX_SEQS];      // node id of a representative boundary
+    __shared__ int s_brep[PLAN_MAX_SEQS], s_blo[PLAN_MAX_SEQS], s_bhi[PLAN_MAX_SEQS];  // per boundary
     __shared__ int s_nbase[PLAN_MAX_SEQS], s_nchunk[PLAN_MAX_SEQS];
     __shared__ int s_seg_units[2 * PLAN_MAX_SEQS];  // internal nodes, then leaves
     __shared__ int s_seg_first[NKINDS][2 * PLAN_MAX_SEQS];  // first unit of each segment in its kind's queue
     __shared__ int smem32[32];
+    __shared__ int s_bcnt[LPT_BUCKETS];
+    __shared__ long long s_scan64[32];
+    __shared__ unsigned s_ktot[NKINDS];  // saturating: each term is clamped to FIELD
     __shared__ int s_nnodes, s_err;
     const int tid = threadIdx.x;
     const int bs = c.block_size;
@@ -200,45 +206,97 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     }
     __syncthreads();
     PLAN_TRACE(2);
-    // LCP-interval tree (one thread, O(n))
-    if (tid == 0) {
-        int sp = 0;           // stack of node ids; the virtual root (-1) has depth 0
-        int* stk = s_nbase;   // stack storage until the bases are computed
-        int nn = 0, npost = 0;
-        s_top[0] = -1;
-        for (int i = 1; i <= n; ++i) {
-            const int h = (i < n) ? s_h[i] : 0;
-            int lo = i - 1;
-            while (sp > 0 && s_ndep[stk[sp - 1]] > h) {
-                const int x = stk[--sp];
-                s_nhi[x] = i - 1;
-                s_post[npost++] = x;
-                lo = s_nlo[x];
-                const int topdep = sp > 0 ? s_ndep[stk[sp - 1]] : 0;
-                if (topdep >= h) s_npar[x] = sp > 0 ? stk[sp - 1] : -1;
-                else s_npar[x] = nn;  // the node about to be pushed with depth h
+    // LCP-interval tree, one thread per boundary b (between sequences b-1 and
+    // b).  A boundary of depth d = h[b] > 0 belongs to the node of depth d
+    // whose interval is the maximal run of boundaries with h >= d around b;
+    // the node's representative is the run's leftmost boundary of depth
+    // exactly d, and node ids number the representatives left to right (the
+    // order in which a left-to-right stack walk would push them).
+    {
+        // one warp per boundary: search 32 boundaries per step with ballots
+        const int warp = tid >> 5, lane = tid & 31;
+        const int nwarps = blockDim.x >> 5;
+        for (int b = 1 + warp; b < n; b += nwarps) {
+            const int d = s_h[b];
+            int rep = 0, lo = 0, hi = 0;
+            if (d > 0) {
+                rep = b;
+                // nearest boundary j < b with h[j] < d (0 stands for "none"); the
+                // leftmost boundary of depth d after it is the representative
+                for (int base = b - 1;; base -= 32) {
+                    const int j = base - lane;
+                    const int hj = j >= 1 ? s_h[j] : 0;
+                    const unsigned less = __ballot_sync(0xffffffffu, j < 1 || hj < d);
+                    unsigned eq = __ballot_sync(0xffffffffu, j >= 1 && hj == d);
+                    if (less) eq &= (1u << (__ffs(less) - 1)) - 1u;
+                    if (eq) rep = base - (31 - __clz(eq));
+                    if (less) {
+                        lo = max(0, base - (__ffs(less) - 1));
+                        break;
+                    }
+                }
+                if (rep == b) {
+                    hi = n - 1;
+                    for (int base = b + 1; base <= n - 1; base += 32) {
+                        const int k = base + lane;
+                        const unsigned less = __ballot_sync(0xffffffffu, k > n - 1 || s_h[min(k, n)] < d);
+                        if (less) {
+                            hi = base + (__ffs(less) - 1) - 1;
+                            break;
+                        }
+                    }
+                }
             }
-            const int topdep = sp > 0 ? s_ndep[stk[sp - 1]] : 0;
-            if (topdep < h) {
-                s_nlo[nn] = lo;
-                s_ndep[nn] = h;
-                s_npar[nn] = -2;
-                stk[sp++] = nn++;
+            if (lane == 0) {
+                s_brep[b] = rep;
+                s_blo[b] = lo;
+                s_bhi[b] = hi;
             }
-            s_top[i] = sp > 0 ? stk[sp - 1] : -1;
         }
-        s_nnodes = nn;
-        // partial ordinals: parents before children (reverse post order)
-        for (int k = npost - 1; k >= 0; --k) {
-            const int x = s_post[k];
+        __syncthreads();
+        const int bnd = tid + 1;
+        const int rep = bnd < n ? s_brep[bnd] : 0;
+        const int lo = bnd < n ? s_blo[bnd] : 0, hi = bnd < n ? s_bhi[bnd] : 0;
+        int nnodes;
+        const bool is_rep = rep != 0 && rep == bnd;
+        const int id = block_exclusive_scan(is_rep ? 1 : 0, &nnodes, smem32);
+        if (is_rep) {
+            s_nid[bnd] = id;
+            s_nlo[id] = lo;
+            s_nhi[id] = hi;
+            s_ndep[id] = s_h[bnd];
+        }
+        __syncthreads();
+        // deepest node covering sequences b-1 and b
+        if (bnd < n) s_top[bnd] = rep ? s_nid[rep] : -1;
+        if (tid == 0) {
+            s_top[0] = -1;
+            s_top[n] = -1;
+            s_nnodes = nnodes;
+        }
+        __syncthreads();
+        // parent: the node of the deeper of the two boundaries bounding the interval
+        for (int x = tid; x < nnodes; x += blockDim.x) {
+            const int xl = s_nlo[x], xh = s_nhi[x];
+            const int hl = xl >= 1 ? s_h[xl] : 0, hr = xh + 1 <= n - 1 ? s_h[xh + 1] : 0;
+            s_npar[x] = (hl == 0 && hr == 0) ? -1 : (hl >= hr ? s_top[xl] : s_top[xh + 1]);
+        }
+        __syncthreads();
+        for (int x = tid; x < nnodes; x += blockDim.x) {
             const int p = s_npar[x];
             const int pdep = p >= 0 ? s_ndep[p] : 0;
             const int ch = seg_chunk(seg_kind(pp, s_nhi[x] - s_nlo[x] + 1));
             s_nchunk[x] = (s_ndep[x] - pdep + ch - 1) / ch;
-            s_nbase[x] = p >= 0 ? s_nbase[p] + s_nchunk[p] : 0;
         }
+        __syncthreads();
+        // partial ordinals: a node's chunks follow those of all its ancestors
+        for (int x = tid; x < nnodes; x += blockDim.x) {
+            int base = 0;
+            for (int p = s_npar[x]; p >= 0; p = s_npar[p]) base += s_nchunk[p];
+            s_nbase[x] = base;
+        }
+        __syncthreads();
     }
-    __syncthreads();
     PLAN_TRACE(3);
     const int nn = s_nnodes;
     const int nseg = nn + n;
@@ -266,17 +324,41 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     }
     __syncthreads();
     PLAN_TRACE(4);
-    // exclusive scans of the unit counts, separately per kernel kind
+    // exclusive scans of the unit counts per kernel kind, packed 21 bits per
+    // kind into one 64-bit scan (a count that does not fit is a plan overflow)
     const int s0 = 2 * tid, s1 = 2 * tid + 1;
     auto kind_of = [&](int s) { return s < nn ? seg_kind(pp, s_nhi[s] - s_nlo[s] + 1) : leaf_kind; };
+    constexpr long long FIELD = 1ll << 21;
+    if (tid < NKINDS) s_ktot[tid] = 0;
+    __syncthreads();
+    {
+        const int k0 = s0 < nseg ? kind_of(s0) : -1, k1 = s1 < nseg ? kind_of(s1) : -1;
+        const unsigned c0 = k0 >= 0 ? (unsigned)min((long long)s_seg_units[s0], FIELD) : 0u;
+        const unsigned c1 = k1 >= 0 ? (unsigned)min((long long)s_seg_units[s1], FIELD) : 0u;
+#pragma unroll
+        for (int kind = 0; kind < NKINDS; ++kind) {
+            const unsigned r = __reduce_add_sync(0xffffffffu, (k0 == kind ? c0 : 0u) + (k1 == kind ? c1 : 0u));
+            if ((tid & 31) == 0 && r) atomicAdd(&s_ktot[kind], r);
+        }
+    }
+    __syncthreads();
+    const bool fits = s_ktot[0] < FIELD && s_ktot[1] < FIELD && s_ktot[2] < FIELD;  // no field can carry
+    if (!fits && tid == 0) s_err = 1;
+    auto packed = [&](int s) -> long long {
+        if (s >= nseg || !fits) return 0;
+        return (long long)s_seg_units[s] << (21 * kind_of(s));
+    };
+    const long long p0 = packed(s0), p1 = packed(s1);
+    long long ptot;
+    const long long pe = block_exclusive_scan64(p0 + p1, &ptot, s_scan64);
     int totals[NKINDS];
 #pragma unroll
     for (int kind = 0; kind < NKINDS; ++kind) {
-        const int c0 = (s0 < nseg && kind_of(s0) == kind) ? s_seg_units[s0] : 0;
-        const int c1 = (s1 < nseg && kind_of(s1) == kind) ? s_seg_units[s1] : 0;
-        const int e = block_exclusive_scan(c0 + c1, &totals[kind], smem32);
+        const int sh = 21 * kind;
+        totals[kind] = (int)((ptot >> sh) & (FIELD - 1));
+        const int e = (int)((pe >> sh) & (FIELD - 1));
         if (s0 < nseg) s_seg_first[kind][s0] = e;
-        if (s1 < nseg) s_seg_first[kind][s1] = e + c0;
+        if (s1 < nseg) s_seg_first[kind][s1] = e + (int)((p0 >> sh) & (FIELD - 1));
     }
     if (tid == 0) {
         for (int kind = 0; kind < NKINDS; ++kind)
@@ -293,47 +375,91 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __syncthreads();
     PLAN_TRACE(5);
     if (s_err) return;
+    // Unit records, written longest first within each tensor-core queue (a
+    // counting sort on the tile count) so that the last units a persistent
+    // CTA claims are the short ones.  Queue order does not change the result:
+    // every unit writes its own (sequence, ordinal, head) partial.
+    auto make_unit = [&](int kind, int u, int* rec) {
+        const int* first = s_seg_first[kind];
+        int lo = 0, hi = nseg - 1;  // last segment whose first unit <= u (zero-count segments precede it)
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (first[mid] <= u) lo = mid; else hi = mid - 1;
+        }
+        const int s = lo, k = u - first[s];
+        if (s < nn) {
+            const int width = s_nhi[s] - s_nlo[s] + 1;
+            const int sk = seg_kind(pp, width);
+            const int spu = seg_spu(pp, sk), chunk = seg_chunk(sk);
+            const int ngroups = (width + spu - 1) / spu;
+            const int ch = k / ngroups, rg = k % ngroups;
+            const int p = s_npar[s];
+            const int pdep = p >= 0 ? s_ndep[p] : 0;
+            rec[0] = s_nlo[s] + rg * spu;
+            rec[1] = min(s_nhi[s], rec[0] + spu - 1);
+            rec[2] = pdep + ch * chunk;
+            rec[3] = min(s_ndep[s], rec[2] + chunk);
+            rec[4] = s_nbase[s] + ch;
+        } else {
+            const int i = s - nn;
+            const int a = s_top[i], b = s_top[i + 1];
+            const int da = a >= 0 ? s_ndep[a] : 0, db = b >= 0 ? s_ndep[b] : 0;
+            const int node = da >= db ? a : b;
+            const int d0 = node >= 0 ? s_ndep[node] : 0;
+            const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
+            const int chunk = seg_chunk(leaf_kind);
+            rec[0] = rec[1] = i;
+            rec[2] = d0 + k * chunk;
+            rec[3] = min(s_len[i], rec[2] + chunk);
+            rec[4] = base + k;
+        }
+    };
+    auto bucket_of = [](const int* rec) { return min(LPT_BUCKETS - 1, (rec[3] - rec[2] - 1) / 128); };
     for (int kind = 0; kind < NKINDS; ++kind) {
         const int total = totals[kind];
-        const int* first = s_seg_first[kind];
+        if (total == 0) continue;  // uniform across the block
         int32_t* units = kind == KIND_FFMA ? ws.units : (kind == KIND_TC ? ws.units_tc : ws.units_tcn);
-        for (int u = tid; u < total; u += blockDim.x) {
-            int lo = 0, hi = nseg - 1;  // last segment whose first unit <= u (zero-count segments precede it)
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (first[mid] <= u) lo = mid; else hi = mid - 1;
+        const bool lpt = kind != KIND_FFMA;
+        const bool one_pass = total <= (int)blockDim.x;  // each thread keeps its record between the passes
+        int mine[5];
+        if (one_pass && tid < total) make_unit(kind, tid, mine);
+        if (lpt) {
+            if (tid < LPT_BUCKETS) s_bcnt[tid] = 0;
+            __syncthreads();
+            for (int u = tid; u < total; u += blockDim.x) {
+                int rec[5];
+                if (one_pass) {
+#pragma unroll
+                    for (int f = 0; f < 5; ++f) rec[f] = mine[f];
+                } else {
+                    make_unit(kind, u, rec);
+                }
+                atomicAdd(&s_bcnt[bucket_of(rec)], 1);
             }
-            const int s = lo, k = u - first[s];
-            int q_lo, q_hi, t0, t1, ord;
-            if (s < nn) {
-                const int width = s_nhi[s] - s_nlo[s] + 1;
-                const int sk = seg_kind(pp, width);
-                const int spu = seg_spu(pp, sk), chunk = seg_chunk(sk);
-                const int ngroups = (width + spu - 1) / spu;
-                const int ch = k / ngroups, rg = k % ngroups;
-                const int p = s_npar[s];
-                const int pdep = p >= 0 ? s_ndep[p] : 0;
-                q_lo = s_nlo[s] + rg * spu;
-                q_hi = min(s_nhi[s], q_lo + spu - 1);
-                t0 = pdep + ch * chunk;
-                t1 = min(s_ndep[s], t0 + chunk);
-                ord = s_nbase[s] + ch;
-            } else {
-                const int i = s - nn;
-                const int a = s_top[i], b = s_top[i + 1];
-                const int da = a >= 0 ? s_ndep[a] : 0, db = b >= 0 ? s_ndep[b] : 0;
-                const int node = da >= db ? a : b;
-                const int d0 = node >= 0 ? s_ndep[node] : 0;
-                const int base = node >= 0 ? s_nbase[node] + s_nchunk[node] : 0;
-                const int chunk = seg_chunk(leaf_kind);
-                q_lo = q_hi = i;
-                t0 = d0 + k * chunk;
-                t1 = min(s_len[i], t0 + chunk);
-                ord = base + k;
+            __syncthreads();
+            if (tid == 0) {
+                int run = 0;
+                for (int b = LPT_BUCKETS - 1; b >= 0; --b) {
+                    const int cnt = s_bcnt[b];
+                    s_bcnt[b] = run;  // cursor: first position of bucket b
+                    run += cnt;
+                }
             }
-            int32_t* U = units + (int64_t)u * UNIT_INTS;
-            U[0] = q_lo; U[1] = q_hi; U[2] = t0; U[3] = t1; U[4] = ord;
+            __syncthreads();
         }
+        for (int u = tid; u < total; u += blockDim.x) {
+            int rec[5];
+            if (one_pass) {
+#pragma unroll
+                for (int f = 0; f < 5; ++f) rec[f] = mine[f];
+            } else {
+                make_unit(kind, u, rec);
+            }
+            const int dst = lpt ? atomicAdd(&s_bcnt[bucket_of(rec)], 1) : u;
+            int32_t* U = units + (int64_t)dst * UNIT_INTS;
+            U[0] = rec[0]; U[1] = rec[1]; U[2] = rec[2]; U[3] = rec[3]; U[4] = rec[4];
+        }
+        __syncthreads();
     }
     __syncthreads();
     PLAN_TRACE(6);
@@ -474,62 +600,66 @@ constexpr int MERGE_MAXP_SMEM = 1024;
 template <typename T, int D>
 __global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts, T* __restrict__ out,
                                              int64_t out_stride) {
+    constexpr int NW = D / 32;
+    constexpr int BATCH = 16;  // independent part loads in flight per thread
     __shared__ float s_w[MERGE_MAXP_SMEM];
-    __shared__ float s_red[D / 32];
-    __shared__ float s_m, s_l;
+    __shared__ float s_rm[NW], s_rl[NW];
+    __shared__ float s_ml[2];
     const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const int P = ws.nparts[i];
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
     const int64_t pstride = (int64_t)Hq * 2;
-    // max of m
-    float m = -INFINITY;
-    for (int p = d; p < P; p += D) m = fmaxf(m, ml[p * pstride]);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_red[warp] = m;
-    __syncthreads();
-    if (d == 0) {
-        float mm = -INFINITY;
-        for (int w2 = 0; w2 < D / 32; ++w2) mm = fmaxf(mm, s_red[w2]);
-        s_m = mm;
-    }
-    __syncthreads();
-    m = s_m;
-    // weights and l
-    float l = 0.f;
+    // (m, l) of all partials combined in one reduction: (m1, l1) + (m2, l2) =
+    // (M, l1 2^(m1 - M) + l2 2^(m2 - M)), M = max(m1, m2)
+    float m = -INFINITY, l = 0.f;
     for (int p = d; p < P; p += D) {
-        const float w = exp2f(ml[p * pstride] - m);
-        if (p < MERGE_MAXP_SMEM) s_w[p] = w;
-        l += ml[p * pstride + 1] * w;
+        const float2 v = *reinterpret_cast<const float2*>(ml + p * pstride);
+        const float mn = fmaxf(m, v.x);
+        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (v.x == -INFINITY ? 0.f : v.y * exp2f(v.x - mn));
+        m = mn;
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    __syncthreads();
-    if (lane == 0) s_red[warp] = l;
-    __syncthreads();
-    if (d == 0) {
-        float ll = 0.f;
-        for (int w2 = 0; w2 < D / 32; ++w2) ll += s_red[w2];
-        s_l = ll;
+    for (int o = 16; o; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+        const float mn = fmaxf(m, m2);
+        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (m2 == -INFINITY ? 0.f : l2 * exp2f(m2 - mn));
+        m = mn;
+    }
+    if (lane == 0) {
+        s_rm[warp] = m;
+        s_rl[warp] = l;
     }
     __syncthreads();
-    l = s_l;
+    if (d == 0) {
+        float mm = s_rm[0], ll = s_rl[0];
+        for (int w2 = 1; w2 < NW; ++w2) {
+            const float m2 = s_rm[w2], l2 = s_rl[w2];
+            const float mn = fmaxf(mm, m2);
+            ll = (mm == -INFINITY ? 0.f : ll * exp2f(mm - mn)) + (m2 == -INFINITY ? 0.f : l2 * exp2f(m2 - mn));
+            mm = mn;
+        }
+        s_ml[0] = mm;
+        s_ml[1] = ll;
+    }
+    __syncthreads();
+    m = s_ml[0];
+    l = s_ml[1];
+    for (int p = d; p < P && p < MERGE_MAXP_SMEM; p += D) s_w[p] = exp2f(ml[p * pstride] - m);
+    __syncthreads();
     const float* po = ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + d;
     const int64_t ostride = (int64_t)Hq * D;
-    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-    int p = 0;
-    for (; p + 4 <= P; p += 4) {
-        const float w0 = p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m);
-        const float w1 = p + 1 < MERGE_MAXP_SMEM ? s_w[p + 1] : exp2f(ml[(p + 1) * pstride] - m);
-        const float w2 = p + 2 < MERGE_MAXP_SMEM ? s_w[p + 2] : exp2f(ml[(p + 2) * pstride] - m);
-        const float w3 = p + 3 < MERGE_MAXP_SMEM ? s_w[p + 3] : exp2f(ml[(p + 3) * pstride] - m);
-        o0 += po[p * ostride] * w0;
-        o1 += po[(p + 1) * ostride] * w1;
-        o2 += po[(p + 2) * ostride] * w2;
-        o3 += po[(p + 3) * ostride] * w3;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int p0 = 0; p0 < P; p0 += BATCH) {
+        float v[BATCH];
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) v[j] = p0 + j < P ? po[(p0 + j) * ostride] : 0.f;
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            const int p = p0 + j;
+            if (p < P) acc[j & 3] += v[j] * (p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m));
+        }
     }
-    for (; p < P; ++p) o0 += po[p * ostride] * (p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m));
-    const float o = (o0 + o1) + (o2 + o3);
+    const float o = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     const float r = (P > 0 && l > 0.f) ? o / l : 0.f;
     out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
 }
@@ -607,10 +737,12 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
         static bool attr = false;
         if (tc_ok && !attr) {
             if (cudaFuncSetAttribute(k_units_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
-                    cudaSuccess ||
-                cudaFuncSetAttribute(k_units_tcn<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TCN_SMEM) !=
-                    cudaSuccess)
+                cudaSuccess)
                 return MENTAT_ERR_CUDA;
+            if constexpr (D == 128)
+                if (cudaFuncSetAttribute(k_units_tcn<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TCN_SMEM) !=
+                    cudaSuccess)
+                    return MENTAT_ERR_CUDA;
             attr = true;
         }
     }
