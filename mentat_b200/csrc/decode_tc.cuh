@@ -1,23 +1,26 @@
 // Tensor-core (tcgen05) decode units for bf16 / fp16 caches, head_dim 64 or 128,
-// KV block 16.  Included by decode_attention.cu; consumes the plan's
-// tensor-core unit queue (segments with >= tc_min_rows query rows: the shared
-// prefixes of a tree).
+// KV block 16.  Included by decode_attention.cu; consumes the plan's wide
+// tensor-core unit queue (segments shared by more than 32 query rows: the
+// shared prefixes of a tree).
 //
-// One CTA per SM (persistent; an issuer warp and two softmax warpgroups; ~193 KB
-// of shared memory).  Per unit and
-// kv head:
+// One CTA per SM (persistent; two softmax warpgroups, an MMA warp and a TMA
+// warp; ~226 KB of shared memory).  Per unit and kv head:
 //   * Q rows of all sharing sequences (up to 256 = two M=128 row tiles) are
 //     written once to shared memory in the K-major 128-byte-swizzled layout.
-//   * K and V come in 64-token tiles (4 blocks) by TMA from the paged pool,
-//     through a 4-stage mbarrier ring, each (block, head) box read once for
-//     every row of the unit.
-//   * S = Q K^T: tcgen05.mma kind::f16, M=128, N=64, K=head_dim, accumulator
+//   * K and V come in 128-token tiles (8 blocks) by TMA from the paged pool,
+//     through separate K (3-stage) and V (2-stage) mbarrier rings, each
+//     (block, head) box read once for every row of the unit.
+//   * S = Q K^T: tcgen05.mma kind::f16, M=128, N=128, K=head_dim, accumulator
 //     in TMEM.  Each thread owns one query row (TMEM lane): scale, mask, online
 //     softmax in base 2 with a lazily raised reference max (O is rescaled in
 //     TMEM only when the row max grows by more than 2^8), P rounded to the
 //     cache dtype and stored back into TMEM over the S columns it came from.
-//   * O += P V: tcgen05.mma with A = P in TMEM, M=128, N=head_dim, K=64
+//   * O += P V: tcgen05.mma with A = P in TMEM, M=128, N=head_dim, K=128
 //     tokens, V read MN-major from shared memory.
+//   * The two row tiles ping-pong: S of row tile r for tile i+1 is issued right
+//     after r's P V(i), so the tensor pipe works on one row tile while the
+//     other's softmax runs.  Issuing S(i+1) after P V(i) also orders the MMAs
+//     so that when S(i+1) is complete, O holds P V(i) and may be rescaled.
 //   * The unnormalised (m, l, o) partial goes to the workspace like the FFMA
 //     units, and k_merge combines both kinds.
 // Every mbarrier wait is bounded by a clock limit; on timeout the CTA records
@@ -38,19 +41,20 @@ __device__ long long g_tc_trace[4096];
 #endif
 
 constexpr int TC_SOFTMAX_WARPS = 8;        // two warpgroups: one per 128-row tile
-constexpr int TC_THREADS = (TC_SOFTMAX_WARPS + 2) * 32;  // + an MMA issuer warp and a TMA producer warp
-constexpr int TC_TILE = 64;                 // tokens per K/V tile (4 blocks of 16)
-constexpr int TC_NST = 4;                   // K/V pipeline stages
+constexpr int TC_THREADS = (TC_SOFTMAX_WARPS + 2) * 32;  // + an MMA warp and a TMA warp
+constexpr int TC_TILE = 128;                // tokens per K/V tile (8 blocks of 16)
+constexpr int TC_KST = 3;                   // K ring stages
+constexpr int TC_VST = 2;                   // V ring stages
 constexpr int TC_RT = 2;                    // row tiles (128 rows each)
 constexpr int TC_Q_BYTES = TC_RT * 2 * 128 * 128;          // 64 KB: [rt][half][128 rows][128 B]
-constexpr int TC_KV_STAGE = 2 * TC_TILE * 128;              // 16 KB: [half][64 tok][128 B]
+constexpr int TC_KV_TILE = 2 * TC_TILE * 128;               // 32 KB: [half][128 tok][128 B]
 constexpr int TC_OFF_Q = 0;
 constexpr int TC_OFF_K = TC_OFF_Q + TC_Q_BYTES;
-constexpr int TC_OFF_V = TC_OFF_K + TC_NST * TC_KV_STAGE;
-constexpr int TC_OFF_BAR = TC_OFF_V + TC_NST * TC_KV_STAGE;  // mbarriers: full[NST], s[2], pv
-constexpr int TC_SMEM = TC_OFF_BAR + 128 + 1024;            // + alignment slack
-constexpr uint32_t TC_TMEM_COLS = 512;      // O[rt] at rt*128, S[buf][rt] at 256 + buf*128 + rt*64
-                                            // (P, packed pairs, overwrites the first 32 columns of its S)
+constexpr int TC_OFF_V = TC_OFF_K + TC_KST * TC_KV_TILE;
+constexpr int TC_OFF_BAR = TC_OFF_V + TC_VST * TC_KV_TILE;  // mbarriers
+constexpr int TC_SMEM = TC_OFF_BAR + 256 + 1024;            // + alignment slack
+constexpr uint32_t TC_TMEM_COLS = 512;      // O[rt] at rt*256, S[rt] at rt*256 + 128
+                                            // (P, packed pairs, overwrites the first 64 columns of its S)
 constexpr long long TC_WAIT_CYCLES = 4000000000ll;  // ~2 s at 1.9 GHz
 
 // ---------------------------------------------------------------------------
@@ -138,6 +142,25 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// the same with the accumulate flag fixed at compile time
+template <bool ACC>
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(ACC ? 1 : 0)
+        : "memory");
+}
+template <bool ACC>
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC ? 1 : 0)
+        : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
@@ -157,6 +180,36 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 64 consecutive fp32 columns of this thread's TMEM lane (two loads, one wait)
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr), "r"(taddr + 32)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 8 / 16 consecutive fp32 columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
     uint32_t r[8];
@@ -265,8 +318,8 @@ template <> struct Pair<__half> {
 };
 
 // Roles: warps 0-3 softmax row tile 0, warps 4-7 softmax row tile 1 (TMEM
-// lane quarter = warp % 4), warp 8 lane 0 issues the MMAs, warp 9 lane 0 the
-// TMA loads.
+// lane quarter = warp % 4), warp 8 lane 0 issues the MMAs, warp 9 the TMA
+// loads (lanes 0-7, one 16-token block each).
 template <typename T, int D>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -277,6 +330,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     constexpr uint32_t IDESC_QK = idesc_f16(FMT, 128, TC_TILE, 0, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(FMT, 128, D, 0, 1);
     constexpr int MAX_BLK = CHUNK_TC / 16 + 1;     // blocks a unit can touch
+    constexpr int BPT = TC_TILE / 16;              // blocks per tile
     extern __shared__ uint8_t tc_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t s_tmem;
@@ -284,24 +338,35 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     __shared__ int s_blk[MAX_BLK];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool issuer = (warp >= TC_SOFTMAX_WARPS);
-    const bool leader = warp == TC_SOFTMAX_WARPS && lane == 0;        // MMA issue
-    const bool producer = warp == TC_SOFTMAX_WARPS + 1 && lane == 0;  // TMA issue
+    const bool leader = warp == TC_SOFTMAX_WARPS && lane == 0;  // MMA issue
+    const bool tma_warp = warp == TC_SOFTMAX_WARPS + 1;         // TMA issue
     const int my_rt = warp >> 2;                       // softmax warps: row tile
     const int my_row = (warp & 3) * 32 + lane;         // row within the tile = TMEM lane
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_full0 = sbase + TC_OFF_BAR;     // [NST] K/V tile landed
-    const uint32_t bar_s0 = bar_full0 + 8 * TC_NST;    // [2] S buffer written
-    const uint32_t bar_pv = bar_s0 + 16;               // P V done
-    const uint32_t bar_empty0 = bar_pv + 8;            // [NST] stage consumed (its P V done)
+    const uint32_t bar_kfull0 = sbase + TC_OFF_BAR;          // [KST] K tile landed
+    const uint32_t bar_kempty0 = bar_kfull0 + 8 * TC_KST;    // [KST] K stage read by every row tile's Q K^T
+    const uint32_t bar_vfull0 = bar_kempty0 + 8 * TC_KST;    // [VST] V tile landed
+    const uint32_t bar_vempty0 = bar_vfull0 + 8 * TC_VST;    // [VST] V stage read by every row tile's P V
+    const uint32_t bar_s0 = bar_vempty0 + 8 * TC_VST;        // [rt] S written (and the row tile's previous P V done)
+    const uint32_t bar_p0 = bar_s0 + 16;                     // [rt] P stored by the row tile's four softmax warps
+    const uint32_t bar_o0 = bar_p0 + 16;                     // [rt] the unit's last P V done
     const int Hkv = c.num_kv_heads, G = Hq / Hkv;
 
     for (int i = tid; i < TC_OFF_BAR / 16; i += TC_THREADS) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
-        for (int st = 0; st < TC_NST; ++st) mbar_init(bar_full0 + 8 * st, 1);
-        mbar_init(bar_s0, 1);
-        mbar_init(bar_s0 + 8, 1);
-        mbar_init(bar_pv, 1);
-        for (int st = 0; st < TC_NST; ++st) mbar_init(bar_empty0 + 8 * st, 1);
+        for (int st = 0; st < TC_KST; ++st) {
+            mbar_init(bar_kfull0 + 8 * st, 1);
+            mbar_init(bar_kempty0 + 8 * st, 1);
+        }
+        for (int st = 0; st < TC_VST; ++st) {
+            mbar_init(bar_vfull0 + 8 * st, 1);
+            mbar_init(bar_vempty0 + 8 * st, 1);
+        }
+        for (int rt = 0; rt < TC_RT; ++rt) {
+            mbar_init(bar_s0 + 8 * rt, 1);
+            mbar_init(bar_p0 + 8 * rt, 4);  // one arrival per softmax warp of the row tile
+            mbar_init(bar_o0 + 8 * rt, 1);
+        }
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -312,12 +377,13 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lane quarter
-    // TMEM columns: O[rt] at rt*128; S[buf][rt] at 256 + buf*128 + rt*64
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
 #endif
-    uint32_t g0 = 0;      // tiles this CTA has processed before the current unit
-    uint32_t issued = 0;  // tiles whose TMA has been issued (producer; global tile index = issue order)
+    // Barrier phases: the K/V rings count tiles (g0); row tile 0 counts every
+    // tile and unit, row tile 1 only those of units with two row tiles.
+    uint32_t g0 = 0, t1 = 0, u0 = 0, u1 = 0;
+    uint32_t issued = 0;  // TMA warp: tiles whose copies have been issued
     const int nunits = ws.hdr[HDR_NTC];
     const int64_t nwork = (int64_t)nunits * Hkv;
     for (;;) {
@@ -334,7 +400,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         const int32_t* tab = table_row(c, layer, slots[q_lo]);
         const int blk0 = t0u / 16, blk_end = (t1u + 15) / 16;
         const int nblk = blk_end - blk0;  // <= MAX_BLK
-        const int ntiles = (nblk + 3) / 4;
+        const int ntiles = (nblk + BPT - 1) / BPT;
 
         for (int j = tid; j < nblk; j += TC_THREADS) s_blk[j] = tab[blk0 + j];
         for (int idx = tid; idx < nrt * 128 * (D / 8); idx += TC_THREADS) {
@@ -350,93 +416,143 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         fence_proxy_async();
         __syncthreads();
         TC_TRACE(1);
+        auto rt_tile = [&](int rt) { return rt == 0 ? g0 : t1; };  // row tile's tile counter at the unit start
+        auto rt_unit = [&](int rt) { return rt == 0 ? u0 : u1; };
 
-        auto issue_tile = [&](int i) {  // producer: TMA of the unit's tile i into stage (g0 + i) % NST
-            const uint32_t stage = (g0 + i) % TC_NST;
-            const int nb = min(4, nblk - 4 * i);
-            const uint32_t bar = bar_full0 + 8 * stage;
-            mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2 * 2048));
-            for (int b = 0; b < nb; ++b) {
-                const int blk = s_blk[4 * i + b];
-                for (int h2 = 0; h2 < HALVES; ++h2) {
-                    const uint32_t off = stage * TC_KV_STAGE + h2 * (TC_TILE * 128) + b * 2048;
-                    tma_load_3d(sbase + TC_OFF_K + off, &tmap_k, bar, h2 * 64, head, blk * 16);
-                    tma_load_3d(sbase + TC_OFF_V + off, &tmap_v, bar, h2 * 64, head, blk * 16);
+        if (tma_warp) {
+            // K(i) then V(i); a stage is reused once every row tile's MMA that read it is done
+            for (int i = 0; i < ntiles; ++i) {
+                const uint32_t gi = g0 + i, ks = gi % TC_KST, vs = gi % TC_VST;
+                const int nb = min(BPT, nblk - BPT * i);
+                const int blk = lane < nb ? s_blk[BPT * i + lane] : 0;
+                int ok = 1;
+                if (lane == 0) {
+                    if (gi >= TC_KST) ok = mbar_wait(bar_kempty0 + 8 * ks, ((gi / TC_KST) - 1) & 1);
+                    if (ok) mbar_expect_tx(bar_kfull0 + 8 * ks, (uint32_t)(nb * HALVES * 2048));
                 }
-            }
-            ++issued;
-        };
-        auto issue_qk = [&](int i) {  // leader: S[(g0+i)%2] = Q K(i)^T once tile i landed
-            const uint32_t g = g0 + i, stage = g % TC_NST;
-            TC_TRACE(1024 + 4 * i);
-            if (!mbar_wait(bar_full0 + 8 * stage, (g / TC_NST) & 1)) {
-                s_abort = 1;
-                return;
-            }
-            TC_TRACE(1025 + 4 * i);
-            tc_fence_after();
-            const uint32_t sbuf = 256 + (g & 1) * 128;
-            for (int rt = 0; rt < nrt; ++rt)
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t qa = sbase + TC_OFF_Q + (rt * 2 + (ks >> 2)) * 16384 + (ks & 3) * 32;
-                    const uint32_t kb = sbase + TC_OFF_K + stage * TC_KV_STAGE + (ks >> 2) * (TC_TILE * 128) + (ks & 3) * 32;
-                    umma_f16(tmem + sbuf + rt * 64, sdesc_sw128(qa, 16, 1024), sdesc_sw128(kb, 16, 1024), IDESC_QK,
-                             ks > 0);
-                }
-            umma_commit(bar_s0 + 8 * (g & 1));
-            TC_TRACE(1026 + 4 * i);
-        };
-        if (producer) {
-            // a stage is reused once the P V of the tile that last used it is done
-            for (int i = 0; i < ntiles && !s_abort; ++i) {
-                const uint32_t gi = g0 + i;
-                if (gi >= TC_NST && !mbar_wait(bar_empty0 + 8 * (gi % TC_NST), ((gi / TC_NST) - 1) & 1)) {
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
                     s_abort = 1;
                     break;
                 }
-#ifdef MENTAT_TC_TRACE
-                if (blockIdx.x == 0 && g_trace_on) g_tc_trace[1536 + i] = clock64();
-#endif
-                issue_tile(i);
+                if (lane < nb)
+#pragma unroll
+                    for (int h2 = 0; h2 < HALVES; ++h2)
+                        tma_load_3d(sbase + TC_OFF_K + ks * TC_KV_TILE + h2 * (TC_TILE * 128) + lane * 2048, &tmap_k,
+                                    bar_kfull0 + 8 * ks, h2 * 64, head, blk * 16);
+                if (lane == 0) {
+                    if (gi >= TC_VST) ok = mbar_wait(bar_vempty0 + 8 * vs, ((gi / TC_VST) - 1) & 1);
+                    if (ok) mbar_expect_tx(bar_vfull0 + 8 * vs, (uint32_t)(nb * HALVES * 2048));
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    s_abort = 1;
+                    ++issued;  // the K copies of this tile are in flight
+                    break;
+                }
+                if (lane < nb)
+#pragma unroll
+                    for (int h2 = 0; h2 < HALVES; ++h2)
+                        tma_load_3d(sbase + TC_OFF_V + vs * TC_KV_TILE + h2 * (TC_TILE * 128) + lane * 2048, &tmap_v,
+                                    bar_vfull0 + 8 * vs, h2 * 64, head, blk * 16);
+                ++issued;
             }
         }
-        if (leader) issue_qk(0);
-
-        float m_ref = -INFINITY, l_sum = 0.f;  // softmax warps: this thread's row
-        const bool wact = !issuer && my_rt < nrt && (my_rt * 128 + (warp & 3) * 32 < R);  // warp-uniform
-        const int row = my_rt * 128 + my_row;
-        int aborted = 0;
-        for (int i = 0; i < ntiles && warp <= TC_SOFTMAX_WARPS; ++i) {
-            const uint32_t g = g0 + i;
-            TC_TRACE(8 + 8 * i);
-            // keep the tensor pipe busy with S(i+1) while tile i's softmax runs
-            if (leader && !s_abort && i + 1 < ntiles) issue_qk(i + 1);
-            TC_TRACE(9 + 8 * i);
-            uint32_t pk[TC_TILE / 2];
-            float fac = 1.f;
-            if (wact) {
-                if (!mbar_wait(bar_s0 + 8 * (g & 1), (g >> 1) & 1)) s_abort = 1;
-                tc_fence_after();
-                TC_TRACE(10 + 8 * i);
-                const int tb = (blk0 + 4 * i) * 16;  // first token of the tile
-                float sv[TC_TILE];
-                tmem_ld32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64, sv);
-                tmem_ld32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64 + 32, sv + 32);
-                float mx = -INFINITY;
-                if (tb >= t0u && tb + TC_TILE <= t1u) {
-#pragma unroll
-                    for (int j = 0; j < TC_TILE; ++j) {
-                        sv[j] *= scale_log2;
-                        mx = fmaxf(mx, sv[j]);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < TC_TILE; ++j) {
-                        const int t = tb + j;
-                        sv[j] = (t >= t0u && t < t1u) ? sv[j] * scale_log2 : -INFINITY;
-                        mx = fmaxf(mx, sv[j]);
-                    }
+        if (leader) {
+            // base descriptors; a K step adds a constant to the start-address field
+            // (16-byte units, no carry: shared memory addresses stay below 256 KB)
+            const uint64_t qd0 = sdesc_sw128(sbase + TC_OFF_Q, 16, 1024);
+            const uint64_t kd0 = sdesc_sw128(sbase + TC_OFF_K, 16, 1024);
+            const uint64_t vd0 = sdesc_sw128(sbase + TC_OFF_V, TC_TILE * 128, 1024);
+            auto issue_qk = [&](int rt, int i) {  // S[rt] = Q_rt K(i)^T
+                const uint32_t g = g0 + i, ks = g % TC_KST;
+                if (rt == 0 && !mbar_wait(bar_kfull0 + 8 * ks, (g / TC_KST) & 1)) {
+                    s_abort = 1;
+                    return;
                 }
+                tc_fence_after();
+                const uint32_t d = tmem + rt * 256 + 128;
+                const uint64_t qd = qd0 + (uint64_t)(rt * 2 * 16384 / 16);
+                const uint64_t kd = kd0 + (uint64_t)(ks * TC_KV_TILE / 16);
+                umma_ss<false>(d, qd, kd, IDESC_QK);
+#pragma unroll
+                for (int k = 1; k < D / 16; ++k)
+                    umma_ss<true>(d, qd + (uint64_t)((k >> 2) * 1024 + (k & 3) * 2),
+                                  kd + (uint64_t)((k >> 2) * (TC_TILE * 8) + (k & 3) * 2), IDESC_QK);
+                umma_commit(bar_s0 + 8 * rt);
+                if (rt == nrt - 1) umma_commit(bar_kempty0 + 8 * ks);
+            };
+            auto issue_pv = [&](int rt, int i) {  // O[rt] += P[rt] V(i)
+                const uint32_t g = g0 + i, vs = g % TC_VST;
+                if (rt == 0 && !mbar_wait(bar_vfull0 + 8 * vs, (g / TC_VST) & 1)) {
+                    s_abort = 1;
+                    return;
+                }
+                tc_fence_after();
+                const uint32_t od = tmem + rt * 256, pa = tmem + rt * 256 + 128;
+                const uint64_t vd = vd0 + (uint64_t)(vs * TC_KV_TILE / 16);
+                umma_f16_ts(od, pa, vd, IDESC_PV, i > 0);
+#pragma unroll
+                for (int k = 1; k < TC_TILE / 16; ++k) umma_ts<true>(od, pa + k * 8, vd + (uint64_t)(k * 2048 / 16), IDESC_PV);
+                if (i == ntiles - 1) umma_commit(bar_o0 + 8 * rt);
+                if (rt == nrt - 1) umma_commit(bar_vempty0 + 8 * vs);
+            };
+            for (int rt = 0; rt < nrt; ++rt) issue_qk(rt, 0);
+            for (int i = 0; i < ntiles && !s_abort; ++i) {
+                TC_TRACE(64 + 8 * i);
+                for (int rt = 0; rt < nrt && !s_abort; ++rt) {
+                    if (!mbar_wait(bar_p0 + 8 * rt, (rt_tile(rt) + i) & 1)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    TC_TRACE(65 + 8 * i + 3 * rt);
+                    issue_pv(rt, i);
+                    TC_TRACE(66 + 8 * i + 3 * rt);
+                    if (i + 1 < ntiles) issue_qk(rt, i + 1);
+                    TC_TRACE(67 + 8 * i + 3 * rt);
+                }
+            }
+        }
+
+        // softmax warps: row tile my_rt, thread = one query row (TMEM lane)
+        float m_ref = -INFINITY, l_sum = 0.f;
+        const bool wact = !issuer && my_rt < nrt;                                   // warp-uniform
+        const bool rows_live = wact && (my_rt * 128 + (warp & 3) * 32 < R);        // warp-uniform
+        const int row = my_rt * 128 + my_row;
+        const uint32_t s_col = tmem + lane_off + my_rt * 256 + 128;
+        const uint32_t o_col = tmem + lane_off + my_rt * 256;
+        for (int i = 0; i < ntiles && wact; ++i) {
+            const uint32_t t = rt_tile(my_rt) + i;
+            TC_TRACE(64 + 8 * i);
+            // warp-collective waits keep the warp converged for the .aligned TMEM accesses
+            if (__any_sync(0xffffffffu, s_abort) || !__all_sync(0xffffffffu, mbar_wait(bar_s0 + 8 * my_rt, t & 1))) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            TC_TRACE(65 + 8 * i);
+            if (rows_live) {
+                const int tb = (blk0 + BPT * i) * 16;  // first token of the tile
+                const bool full = tb >= t0u && tb + TC_TILE <= t1u;
+                // scaled, masked score of token j of the tile
+                auto score = [&](float x, int j) {
+                    return (full || (tb + j >= t0u && tb + j < t1u)) ? x * scale_log2 : -INFINITY;
+                };
+                // tokens 64-127 stay in registers; tokens 0-63 are read for the max
+                // here and again, 32 at a time, for their probabilities
+                float hi[64];
+                float mx = -INFINITY;
+                {
+                    float lo[64];
+                    tmem_ld64(s_col, lo);
+#pragma unroll
+                    for (int j = 0; j < 64; ++j) mx = fmaxf(mx, score(lo[j], j));
+                }
+                tmem_ld64(s_col + 64, hi);
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    hi[j] = score(hi[j], 64 + j);
+                    mx = fmaxf(mx, hi[j]);
+                }
+                float fac = 1.f;
                 const float m_new = fmaxf(m_ref, mx);
                 if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
                     if (m_ref != -INFINITY) {
@@ -445,68 +561,73 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     }
                     m_ref = m_new;
                 }
-                float acc = 0.f;
-#pragma unroll
-                for (int e = 0; e < TC_TILE / 2; ++e) {
-                    const float a = ex2_approx(sv[2 * e] - m_ref), b = ex2_approx(sv[2 * e + 1] - m_ref);
-                    acc += a + b;
-                    pk[e] = Pair<T>::pack(a, b);
-                }
-                l_sum += acc;
-                TC_TRACE(11 + 8 * i);
-                // P over the consumed S columns; P V(i-1) read the other S buffer, so no wait is needed
-                tmem_st32(tmem + lane_off + 256 + (g & 1) * 128 + my_rt * 64, reinterpret_cast<const float*>(pk));
-                TC_TRACE(12 + 8 * i);
-                // rows whose reference max rose rescale O, after P V(i-1) is done
+                // rows whose reference max rose rescale O; S(i) being complete means
+                // P V(i-1) of this row tile is complete too (issued before S(i))
                 if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
-                    if (!mbar_wait(bar_pv, (g - 1) & 1)) s_abort = 1;
-                    tc_fence_after();
                     const float f = row < R ? fac : 1.f;
 #pragma unroll
                     for (int cb = 0; cb < D / 32; ++cb) {
                         float ov[32];
-                        tmem_ld32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
+                        tmem_ld32(o_col + cb * 32, ov);
 #pragma unroll
                         for (int k = 0; k < 32; ++k) ov[k] *= f;
-                        tmem_st32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
+                        tmem_st32(o_col + cb * 32, ov);
                     }
                 }
-                TC_TRACE(13 + 8 * i);
+                // P (pairs packed in one column) over the consumed S columns: the P of
+                // tokens 0-63 lands in columns 0-31, that of tokens 64-127 in 32-63,
+                // each written after the S columns it overwrites have been read
+                float acc = 0.f;
+#pragma unroll
+                for (int cchunk = 0; cchunk < 2; ++cchunk) {
+                    float v[32];
+                    tmem_ld32(s_col + 32 * cchunk, v);
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float a = ex2_approx(score(v[2 * e], 32 * cchunk + 2 * e) - m_ref);
+                        const float b = ex2_approx(score(v[2 * e + 1], 32 * cchunk + 2 * e + 1) - m_ref);
+                        acc += a + b;
+                        pk[e] = Pair<T>::pack(a, b);
+                    }
+                    tmem_st16(s_col + 16 * cchunk, pk);
+                }
+#pragma unroll
+                for (int cchunk = 0; cchunk < 2; ++cchunk) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float a = ex2_approx(hi[32 * cchunk + 2 * e] - m_ref);
+                        const float b = ex2_approx(hi[32 * cchunk + 2 * e + 1] - m_ref);
+                        acc += a + b;
+                        pk[e] = Pair<T>::pack(a, b);
+                    }
+                    tmem_st16(s_col + 32 + 16 * cchunk, pk);
+                }
+                tmem_st_wait();
+                l_sum += acc;
+                TC_TRACE(66 + 8 * i);
             }
             tc_fence_before();
-            aborted = bar_sync_or(TC_SOFTMAX_WARPS * 32 + 32, s_abort);  // P(i) stored (softmax warps + issuer)
-            TC_TRACE(14 + 8 * i);
-            if (aborted) break;
-            if (leader) {  // O += P V(i)
-                tc_fence_after();
-                const uint32_t stage = g % TC_NST;
-                for (int rt = 0; rt < nrt; ++rt)
-                    for (int ks = 0; ks < TC_TILE / 16; ++ks) {
-                        const uint32_t pa = tmem + 256 + (g & 1) * 128 + rt * 64 + ks * 8;
-                        const uint32_t vb = sbase + TC_OFF_V + stage * TC_KV_STAGE + ks * 2048;
-                        umma_f16_ts(tmem + rt * 128, pa, sdesc_sw128(vb, TC_TILE * 128, 1024), IDESC_PV,
-                                    (i > 0 || ks > 0));
-                    }
-                umma_commit(bar_pv);
-                umma_commit(bar_empty0 + 8 * stage);
-            }
-            TC_TRACE(15 + 8 * i);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_p0 + 8 * my_rt);
+            TC_TRACE(67 + 8 * i);
         }
         // every thread reaches this CTA-wide barrier, so the abort decision is uniform
-        if (__syncthreads_or(aborted || s_abort)) {
+        if (__syncthreads_or(s_abort)) {
             s_abort = 1;
             break;
         }
-        // last P V done -> partials of this thread's row
-        if (wact) {
-            if (!mbar_wait(bar_pv, (g0 + ntiles - 1) & 1)) s_abort = 1;
+        // the unit's last P V of this row tile done -> partials of this thread's row
+        if (rows_live) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar_o0 + 8 * my_rt, rt_unit(my_rt) & 1))) s_abort = 1;
             tc_fence_after();
             const int seq = q_lo + row / G, hq = head * G + row % G;
             const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
 #pragma unroll
             for (int cb = 0; cb < D / 32; ++cb) {
                 float ov[32];
-                tmem_ld32(tmem + lane_off + my_rt * 128 + cb * 32, ov);
+                tmem_ld32(o_col + cb * 32, ov);
                 if (row < R) {
                     float4* dst = reinterpret_cast<float4*>(ws.part_o + pi * D + cb * 32);
 #pragma unroll
@@ -518,13 +639,20 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 ws.part_ml[pi * 2 + 1] = l_sum;
             }
         } else if (leader) {
-            if (!mbar_wait(bar_pv, (g0 + ntiles - 1) & 1)) s_abort = 1;  // keep the phase count of every waiter in step
+            // the unit's last P V must be complete before the next unit's first MMA overwrites O
+            for (int rt = 0; rt < nrt; ++rt)
+                if (!mbar_wait(bar_o0 + 8 * rt, rt_unit(rt) & 1)) s_abort = 1;
         }
         TC_TRACE(4);
 #ifdef MENTAT_TC_TRACE
         g_trace_on = false;
 #endif
         g0 += ntiles;
+        u0 += 1;
+        if (nrt > 1) {
+            t1 += ntiles;
+            u1 += 1;
+        }
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
@@ -533,10 +661,12 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     __syncthreads();
     if (s_abort) {
         if (leader) atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
-        if (producer) {
-            // at most NST tiles can be issued and not yet waited for
-            for (uint32_t k = issued > TC_NST ? issued - TC_NST : 0; k < issued; ++k)
-                (void)mbar_wait(bar_full0 + 8 * (k % TC_NST), (k / TC_NST) & 1);
+        if (tma_warp && lane == 0) {
+            // at most KST K tiles and VST V tiles can be issued and not yet waited for
+            for (uint32_t k = issued > TC_KST ? issued - TC_KST : 0; k < issued; ++k)
+                (void)mbar_wait(bar_kfull0 + 8 * (k % TC_KST), (k / TC_KST) & 1);
+            for (uint32_t k = issued > TC_VST ? issued - TC_VST : 0; k < issued; ++k)
+                (void)mbar_wait(bar_vfull0 + 8 * (k % TC_VST), (k / TC_VST) & 1);
         }
         __syncthreads();
     }

@@ -134,6 +134,38 @@ class PagedKV:
         return k if self.which == "k" else v
 
 
+class _PinnedRing:
+    """Small host-to-device int32 uploads through reused page-locked buffers.
+
+    Each step's sequence lengths change, so a fresh pinned tensor per upload
+    would keep the pinned-memory allocator busy; a buffer here is rewritten
+    only after the copy that last read it has completed (its event).
+    """
+
+    def __init__(self, device, depth: int = 16, cap: int = 1024):
+        self.device = device
+        self.bufs = [torch.empty(cap, dtype=torch.int32, pin_memory=True) for _ in range(depth)]
+        self.events = [None] * depth
+        self.i = 0
+
+    def upload(self, values: torch.Tensor) -> torch.Tensor:
+        n = values.numel()
+        k = self.i
+        self.i = (k + 1) % len(self.bufs)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        if self.bufs[k].numel() < n:
+            self.bufs[k] = torch.empty(max(n, 2 * self.bufs[k].numel()), dtype=torch.int32, pin_memory=True)
+        buf = self.bufs[k][:n]
+        buf.copy_(values)
+        dev = torch.empty(n, dtype=torch.int32, device=self.device)
+        dev.copy_(buf, non_blocking=True)
+        ev = self.events[k] if self.events[k] is not None else torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.events[k] = ev
+        return dev
+
+
 class PagedKVCacheManager:
     """``PagedKVCacheManager`` (``core/paged_kv_cache.py:102-455``) on the device."""
 
@@ -206,6 +238,7 @@ class PagedKVCacheManager:
         self._next_seq_id = 0
         self._cache: dict = {}
         self._ws = None
+        self._uploads = _PinnedRing(self.device)
         self._ws_bytes = 0
 
     # ------------------------------------------------------------------ util
@@ -250,14 +283,12 @@ class PagedKVCacheManager:
 
     def _slots_dev(self, seq_ids) -> torch.Tensor:
         def make():
-            host = torch.tensor([self._sequences[s].slot for s in seq_ids], dtype=torch.int32, pin_memory=True)
-            return host.to(self.device, non_blocking=True)
+            return self._uploads.upload(torch.tensor([self._sequences[s].slot for s in seq_ids], dtype=torch.int32))
         return self._remember(("slots",) + tuple(seq_ids), make)
 
     def _cu_seqlens(self, lens) -> torch.Tensor:
         def make():
-            host = torch.tensor([0] + list(lens), dtype=torch.int32).cumsum(0, dtype=torch.int32)
-            return host.pin_memory().to(self.device, non_blocking=True)
+            return self._uploads.upload(torch.tensor([0] + list(lens), dtype=torch.int32).cumsum(0, dtype=torch.int32))
         return self._remember(("cu",) + tuple(lens), make)
 
     # ------------------------------------------------------------- sequences
