@@ -226,17 +226,27 @@ def run_mentat(args):
     time.sleep(0.3)
 
     # device-resident timing: one attn_decode per step
-    _lib.check(lib.mentat_profile_enable(min(args.steps, 4096)), "mentat_profile_enable")
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.mentat_kernel_launch_count()
     e0.record()
     for _ in range(args.steps):
         attn_decode(q, k, v, None, cu, mx, NBR)
     e1.record()
+    launches = lib.mentat_kernel_launch_count() - launches0
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    m.check()
+
+    # per-kernel durations for the roofline: a second pass with CUDA events
+    # recorded between the kernels of every call (which keeps them from
+    # overlapping, so this pass is not the headline number)
+    prof_steps = min(args.steps, 50)
+    _lib.check(lib.mentat_profile_enable(prof_steps), "mentat_profile_enable")
+    for _ in range(prof_steps):
+        attn_decode(q, k, v, None, cu, mx, NBR)
     stage = (ctypes.c_double * 5)()
     cnt = ctypes.c_int32()
     _lib.check(lib.mentat_profile_collect(stage, ctypes.byref(cnt)), "mentat_profile_collect")
@@ -331,7 +341,7 @@ def run_mentat(args):
                     "d2h_bytes_per_step": int(out_host.numel() * 2),
                     "path": "pinned H2D q + new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
                             "D2H output"},
-            "gpu_launches": 6 * args.steps,  # lcp, plan, FFMA units, wide + narrow tensor-core units, merge
+            "gpu_launches": int(launches),  # counted by the library over the device-timed loop
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

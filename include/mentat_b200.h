@@ -177,6 +177,11 @@ int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t layer, const i
 int mentat_profile_enable(int32_t max_records);
 int mentat_profile_collect(double* stage_ms, int32_t* launches);
 
+/* Number of kernels this library has launched since it was loaded (all entry
+ * points, devices and streams).  No counterpart in the reference; the
+ * benchmark reads it around its timed region. */
+int64_t mentat_kernel_launch_count(void);
+
 /*
  * Fused entropy gate over the full vocabulary, one leaf per row.  Replaces
  * compute_entropy (generator_utils.py:196-202), apply_repetition_penalty

@@ -8,15 +8,32 @@
 
 #include "../../include/mentat_b200.h"
 
-#define MENTAT_CHECK_LAUNCH()                          \
-    do {                                               \
-        if (cudaPeekAtLastError() != cudaSuccess) {    \
-            (void)cudaGetLastError();                  \
-            return MENTAT_ERR_CUDA;                    \
-        }                                              \
+#include <atomic>
+
+namespace mentat {
+// kernels this library has launched (host counter, all devices and streams)
+inline std::atomic<long long> g_kernel_launches{0};
+}  // namespace mentat
+
+// follows every kernel launch: counts it and turns a launch error into a status
+#define MENTAT_CHECK_LAUNCH()                                                 \
+    do {                                                                      \
+        mentat::g_kernel_launches.fetch_add(1, std::memory_order_relaxed);    \
+        if (cudaPeekAtLastError() != cudaSuccess) {                           \
+            (void)cudaGetLastError();                                         \
+            return MENTAT_ERR_CUDA;                                           \
+        }                                                                     \
     } while (0)
 
 namespace mentat {
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while its predecessor on the stream still runs;
+// griddep_wait() returns once that predecessor has completed and its writes
+// are visible (at once for an ordinary launch), and griddep_launch() lets the
+// next such kernel on the stream be scheduled.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // element types

@@ -77,63 +77,63 @@ __host__ __device__ inline void ws_carve(void* base, int n, int hq, int d, int m
 }
 
 // ---------------------------------------------------------------------------
-// 1. plan
-// ---------------------------------------------------------------------------
-// ---------------------------------------------------------------------------
-// 0. first differing table entry of each adjacent pair, grid-wide:
-//    block (chunk, pair) compares LCP_CHUNK entries, atomicMin into ws.lcp
-//    (reset to a large value by a memset before the launch)
+// 0. first differing table entry of each adjacent pair: one block per pair
+//    walks the two table rows LCP_CHUNK entries at a time and writes the first
+//    differing block index (INT_MAX: none) to ws.lcp
 // ---------------------------------------------------------------------------
 constexpr int LCP_THREADS = 256;
 constexpr int LCP_CHUNK = LCP_THREADS * 16;
 __global__ void __launch_bounds__(LCP_THREADS) k_lcp(mentat_kv_cache c, int layer, const int32_t* slots, int n,
                                                      DecodeWs ws) {
     __shared__ int s_min[LCP_THREADS / 32];
-    const int pair = blockIdx.y + 1;  // compares sequences pair-1 and pair
+    griddep_wait();  // tables and lengths may come from the previous launch on the stream
+    griddep_launch();
+    const int pair = blockIdx.x + 1;  // compares sequences pair-1 and pair
     if (pair >= n) return;
     int sa = slots[pair - 1], sb = slots[pair];
     if (sa < 0 || sa >= c.max_seqs) sa = 0;
     if (sb < 0 || sb >= c.max_seqs) sb = 0;
-    if (sa == sb) return;
+    if (sa == sb) return;  // the plan does not read this pair
     const int bs = c.block_size;
     const int la = c.ntok[seq_index(c, layer, sa)], lb = c.ntok[seq_index(c, layer, sb)];
     const int m = min((la + bs - 1) / bs, (lb + bs - 1) / bs);
-    const int j0 = blockIdx.x * LCP_CHUNK;
-    if (j0 >= m) return;
     const int32_t* ta = table_row(c, layer, sa);
     const int32_t* tb = table_row(c, layer, sb);
-    int first = INT_MAX;
     // 16-byte loads only when every row is 16-byte aligned, so a load never crosses a row end
     const bool vec = (c.max_blocks_per_seq & 3) == 0 && ((((uintptr_t)ta) | ((uintptr_t)tb)) & 15) == 0;
-    if (vec) {
+    int first = INT_MAX;
+    // chunks in order; the first chunk with a difference holds the answer
+    for (int j0 = 0; j0 < m && first == INT_MAX; j0 += LCP_CHUNK) {
+        int f = INT_MAX;
+        if (vec) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = j0 + (u * LCP_THREADS + threadIdx.x) * 4;
-            if (j < m) {
-                const int4 a = *reinterpret_cast<const int4*>(ta + j);
-                const int4 b = *reinterpret_cast<const int4*>(tb + j);
-                if (a.x != b.x) first = min(first, j);
-                else if (a.y != b.y && j + 1 < m) first = min(first, j + 1);
-                else if (a.z != b.z && j + 2 < m) first = min(first, j + 2);
-                else if (a.w != b.w && j + 3 < m) first = min(first, j + 3);
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + (u * LCP_THREADS + threadIdx.x) * 4;
+                if (j < m) {
+                    const int4 a = *reinterpret_cast<const int4*>(ta + j);
+                    const int4 b = *reinterpret_cast<const int4*>(tb + j);
+                    if (a.x != b.x) f = min(f, j);
+                    else if (a.y != b.y && j + 1 < m) f = min(f, j + 1);
+                    else if (a.z != b.z && j + 2 < m) f = min(f, j + 2);
+                    else if (a.w != b.w && j + 3 < m) f = min(f, j + 3);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int j = j0 + u * LCP_THREADS + threadIdx.x;
+                if (j < m && ta[j] != tb[j]) f = min(f, j);
             }
         }
-    } else {
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int j = j0 + u * LCP_THREADS + threadIdx.x;
-            if (j < m && ta[j] != tb[j]) first = min(first, j);
-        }
-    }
+        for (int o = 16; o; o >>= 1) f = min(f, __shfl_xor_sync(0xffffffffu, f, o));
+        if ((threadIdx.x & 31) == 0) s_min[threadIdx.x >> 5] = f;
+        __syncthreads();
 #pragma unroll
-    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
-    if ((threadIdx.x & 31) == 0) s_min[threadIdx.x >> 5] = first;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int f = INT_MAX;
-        for (int w = 0; w < LCP_THREADS / 32; ++w) f = min(f, s_min[w]);
-        if (f != INT_MAX) atomicMin(&ws.lcp[pair], f);
+        for (int w = 0; w < LCP_THREADS / 32; ++w) first = min(first, s_min[w]);
+        __syncthreads();
     }
+    if (threadIdx.x == 0) ws.lcp[pair] = first;
 }
 
 // Plan parameters for one launch.  A segment (node of the LCP-interval tree or
@@ -181,6 +181,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __shared__ int s_nnodes, s_err;
     const int tid = threadIdx.x;
     const int bs = c.block_size;
+    griddep_wait();  // the pair LCPs
+    griddep_launch();
     PLAN_TRACE(0);
 
     for (int i = tid; i < n; i += blockDim.x) {
@@ -484,6 +486,8 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
     __shared__ float m_s[MAX_ROWS], l_s[MAX_ROWS], a_s[MAX_ROWS];
     __shared__ float red_s[TS > 1 ? TS : 1][TS > 1 ? MAX_ROWS : 1][TS > 1 ? D : 1];
     __shared__ int s_work;
+    griddep_wait();  // the plan
+    griddep_launch();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hkv = c.num_kv_heads, G = Hq / Hkv, bs = c.block_size;
     const int nunits = ws.hdr[HDR_NSIMT];
@@ -605,6 +609,8 @@ __global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts,
     __shared__ float s_w[MERGE_MAXP_SMEM];
     __shared__ float s_rm[NW], s_rl[NW];
     __shared__ float s_ml[2];
+    griddep_wait();  // every unit kernel's partials
+    griddep_launch();
     const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const int P = ws.nparts[i];
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
@@ -720,6 +726,34 @@ static bool narrow_enabled() {
     return v != 0;
 }
 
+// Decode kernels go out with programmatic stream serialization: each may be
+// scheduled while its predecessor on the stream runs, and waits for it with
+// griddep_wait (the narrow kernel waits for the wide one only at its end).
+// MENTAT_PDL=0 launches them one after another instead.
+static bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MENTAT_PDL");
+        v = (e && *e) ? (atoi(e) != 0) : 1;
+    }
+    return v != 0;
+}
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 template <typename T, int D>
 static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,
                          int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
@@ -748,40 +782,48 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     }
     PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows()};
     prof_mark(0, s);
+    const bool pdl = pdl_enabled();
     if (n > 1) {
-        if (cudaMemsetAsync(ws.lcp, 0x7F, sizeof(int32_t) * n, s) != cudaSuccess) return MENTAT_ERR_CUDA;
-        dim3 lg((c->max_blocks_per_seq + LCP_CHUNK - 1) / LCP_CHUNK, n - 1);
-        k_lcp<<<lg, LCP_THREADS, 0, s>>>(*c, layer, slots, n, ws);
+        if (launch(pdl, k_lcp, dim3(n - 1), dim3(LCP_THREADS), 0, s, *c, layer, slots, n, ws) != cudaSuccess)
+            return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
     }
-    k_plan<<<1, 1024, 0, s>>>(*c, layer, slots, n, pp, ws, max_parts);
+    if (launch(pdl, k_plan, dim3(1), dim3(1024), 0, s, *c, layer, slots, n, pp, ws, max_parts) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     prof_mark(1, s);
     const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
-    k_units<T, D><<<num_sms() * 4, UNIT_THREADS, 0, s>>>(*c, layer, slots, reinterpret_cast<const T*>(q), q_stride,
-                                                         Hq, qscale, ws, max_parts);
-    MENTAT_CHECK_LAUNCH();
+    const T* qt = reinterpret_cast<const T*>(q);
+    // a segment has at least G query rows, so with the tensor-core path on and
+    // tc_min_rows <= G no unit can land in the FFMA queue
+    if (!(tc_ok && tc_min_rows() <= G)) {
+        if (launch(pdl, k_units<T, D>, dim3(num_sms() * 4), dim3(UNIT_THREADS), 0, s, *c, layer, slots, qt, q_stride,
+                   Hq, qscale, ws, max_parts) != cudaSuccess)
+            return MENTAT_ERR_CUDA;
+        MENTAT_CHECK_LAUNCH();
+    }
     prof_mark(2, s);
     if constexpr (!std::is_same<T, float>::value) {
         if (tc_ok) {
-            k_units_tc<T, D><<<num_sms(), TC_THREADS, TC_SMEM, s>>>(maps->mk, maps->mv, *c, layer, slots,
-                                                                    reinterpret_cast<const T*>(q), q_stride, Hq,
-                                                                    qscale, ws, max_parts);
+            if (launch(pdl, k_units_tc<T, D>, dim3(num_sms()), dim3(TC_THREADS), TC_SMEM, s, maps->mk, maps->mv, *c,
+                       layer, slots, qt, q_stride, Hq, qscale, ws, max_parts) != cudaSuccess)
+                return MENTAT_ERR_CUDA;
             MENTAT_CHECK_LAUNCH();
         }
     }
     prof_mark(3, s);
     if constexpr (!std::is_same<T, float>::value && D == 128) {
         if (narrow_ok) {
-            k_units_tcn<T, D><<<num_sms(), TCN_THREADS, TCN_SMEM, s>>>(maps->mk, maps->mv, *c, layer, slots,
-                                                                       reinterpret_cast<const T*>(q), q_stride, Hq,
-                                                                       qscale, ws, max_parts);
+            if (launch(pdl, k_units_tcn<T, D>, dim3(num_sms()), dim3(TCN_THREADS), TCN_SMEM, s, maps->mk, maps->mv,
+                       *c, layer, slots, qt, q_stride, Hq, qscale, ws, max_parts) != cudaSuccess)
+                return MENTAT_ERR_CUDA;
             MENTAT_CHECK_LAUNCH();
         }
     }
     prof_mark(4, s);
-    dim3 mg(n, Hq);
-    k_merge<T, D><<<mg, D, 0, s>>>(Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride);
+    if (launch(pdl, k_merge<T, D>, dim3(n, Hq), dim3(D), 0, s, Hq, ws, max_parts, reinterpret_cast<T*>(out),
+               out_stride) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     prof_mark(5, s);
     if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;

@@ -100,6 +100,9 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void bar_sync_id(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 // named barrier 1 over `count` threads that also ORs a flag across them
 __device__ __forceinline__ int bar_sync_or(int count, int flag) {
     uint32_t out;
@@ -377,6 +380,10 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lane quarter
+    // The set-up above overlaps the plan; the plan's units are read below.  The
+    // narrow kernel after this one may start on the SMs this one leaves free.
+    griddep_wait();
+    griddep_launch();
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
 #endif
@@ -402,19 +409,49 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         const int nblk = blk_end - blk0;  // <= MAX_BLK
         const int ntiles = (nblk + BPT - 1) / BPT;
 
-        for (int j = tid; j < nblk; j += TC_THREADS) s_blk[j] = tab[blk0 + j];
-        for (int idx = tid; idx < nrt * 128 * (D / 8); idx += TC_THREADS) {
-            const int r = idx / (D / 8), ch = idx % (D / 8);
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < R) {
-                const int seq = q_lo + r / G, g = r % G;
-                v = *reinterpret_cast<const uint4*>(q + (int64_t)seq * q_stride + (int64_t)(head * G + g) * D + ch * 8);
+        // The TMA warp reads the unit's block ids and starts streaming K/V at
+        // once; the other warps stage Q meanwhile (all loads in flight together)
+        // and meet on named barrier 2 before the first MMA.
+        if (tma_warp) {
+            constexpr int PER_LANE = (MAX_BLK + 31) / 32;
+            int b[PER_LANE];
+#pragma unroll
+            for (int k = 0; k < PER_LANE; ++k) b[k] = lane + 32 * k < nblk ? tab[blk0 + lane + 32 * k] : 0;
+#pragma unroll
+            for (int k = 0; k < PER_LANE; ++k)
+                if (lane + 32 * k < nblk) s_blk[lane + 32 * k] = b[k];
+            __syncwarp();
+        } else {
+            constexpr int QCH = 2 * 128 * (D / 8);                  // 16-byte Q chunks of two row tiles
+            constexpr int NQ = TC_THREADS - 32;                     // loading threads (TMA warp excluded)
+            constexpr int QB = 8;                                   // loads in flight per thread
+            const int qt = tid;  // 0 .. NQ-1: the TMA warp is the last warp
+            const int nq = nrt * 128 * (D / 8);
+#pragma unroll 1
+            for (int base = 0; base < QCH; base += NQ * QB) {
+                uint4 v[QB];
+#pragma unroll
+                for (int k = 0; k < QB; ++k) {
+                    const int idx = base + qt + NQ * k, r = idx / (D / 8), ch = idx % (D / 8);
+                    v[k] = make_uint4(0, 0, 0, 0);
+                    if (idx < nq && r < R) {
+                        const int seq = q_lo + r / G, g = r % G;
+                        v[k] = *reinterpret_cast<const uint4*>(q + (int64_t)seq * q_stride + (int64_t)(head * G + g) * D +
+                                                               ch * 8);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < QB; ++k) {
+                    const int idx = base + qt + NQ * k, r = idx / (D / 8), ch = idx % (D / 8);
+                    if (idx < nq) {
+                        const int rt = r >> 7, rr = r & 127, half = ch >> 3;
+                        *reinterpret_cast<uint4*>(smem + TC_OFF_Q + (rt * 2 + half) * 16384 + sw128_off(rr, ch & 7)) = v[k];
+                    }
+                }
             }
-            const int rt = r >> 7, rr = r & 127, half = ch >> 3;
-            *reinterpret_cast<uint4*>(smem + TC_OFF_Q + (rt * 2 + half) * 16384 + sw128_off(rr, ch & 7)) = v;
+            fence_proxy_async();
+            bar_sync_id(2, TC_THREADS - 32);
         }
-        fence_proxy_async();
-        __syncthreads();
         TC_TRACE(1);
         auto rt_tile = [&](int rt) { return rt == 0 ? g0 : t1; };  // row tile's tile counter at the unit start
         auto rt_unit = [&](int rt) { return rt == 0 ? u0 : u1; };

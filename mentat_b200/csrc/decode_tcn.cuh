@@ -75,9 +75,6 @@ __device__ __forceinline__ int bar_sync_or_id(int id, int count, int flag) {
         : "memory");
     return (int)out;
 }
-__device__ __forceinline__ void bar_sync_id(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(TCN_THREADS, 1)
@@ -130,6 +127,11 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    // Launched after the wide kernel, which waited for the plan before it let
+    // this one start: the plan is complete here.  This kernel does not wait for
+    // the wide one until its end, so the two overlap on the SMs the wide kernel
+    // leaves free.
+    griddep_launch();
 
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
@@ -451,6 +453,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     if (warp == 0) tmem_dealloc(tmem, TCN_TMEM_COLS);
+    griddep_wait();  // complete only after the wide kernel: the merge reads both kernels' partials
 }
 
 }  // namespace mentat

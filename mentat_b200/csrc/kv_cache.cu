@@ -523,6 +523,9 @@ static bool bad_cache(const mentat_kv_cache* c) {
 
 extern "C" {
 
+int64_t mentat_kernel_launch_count(void) { return (int64_t)mentat::g_kernel_launches.load(std::memory_order_relaxed); }
+
+
 int mentat_abi_version(void) { return MENTAT_ABI_VERSION; }
 
 const char* mentat_status_string(int s) {
