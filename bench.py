@@ -115,25 +115,56 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def build_tree(seed, device, extra_blocks):
+def build_shape(prefix, suf, seed, device, extra_blocks):
+    """A shared prefix forked into len(suf) branches with the given own lengths."""
     from mentat_b200 import PagedKVCacheManager
-    suf = suffixes(seed)
-    blocks = PREFIX // BS + int(sum((s + BS - 1) // BS for s in suf)) + extra_blocks + 16
+    nbr = len(suf)
+    blocks = prefix // BS + int(sum((s + BS - 1) // BS for s in suf)) + extra_blocks + 16
     m = PagedKVCacheManager(1, HKV, D, max_blocks=blocks, block_size=BS, device=device, dtype=torch.bfloat16,
-                            max_seqs=NBR + 2)
+                            max_seqs=nbr + 2)
     g = torch.Generator(device=device).manual_seed(seed)
     kv = lambda n: torch.randn((n, HKV, D), generator=g, device=device).to(torch.bfloat16)  # noqa: E731
     root = m.allocate_sequence()
-    for a in range(0, PREFIX, 8192):
-        n = min(8192, PREFIX - a)
+    for a in range(0, prefix, 8192):
+        n = min(8192, prefix - a)
         m.append_tokens(root, 0, kv(n), kv(n))
-    kids = [m.fork_sequence(root) for _ in range(NBR)]
+    kids = [m.fork_sequence(root) for _ in range(nbr)]
     m.free_sequence(root)
     for kid, n in zip(kids, suf):
         m.append_tokens(kid, 0, kv(int(n)), kv(int(n)))
-    q = torch.randn((NBR, HQ, D), generator=g, device=device).to(torch.bfloat16)
+    q = torch.randn((nbr, HQ, D), generator=g, device=device).to(torch.bfloat16)
     m.check()
+    return m, kids, q
+
+
+def build_tree(seed, device, extra_blocks):
+    suf = suffixes(seed)
+    m, kids, q = build_shape(PREFIX, suf, seed, device, extra_blocks)
     return m, kids, q, suf
+
+
+def run_profile_case(args):
+    """A smaller tree for a profiler capture: warm-up calls, then --steps decode
+    calls of attn_decode; prints the mean time per call (no JSON line)."""
+    from mentat_b200.attention_backend import attn_decode
+    prefix, nbr, suffix = (int(x) for x in args.profile_case.split(","))
+    device = torch.device("cuda", 0)
+    m, kids, q = build_shape(prefix, [suffix] * nbr, args.seed, device, 0)
+    k, v, cu, mx = m.build_packed_kv(kids, 0)
+    for _ in range(args.warmup):
+        attn_decode(q, k, v, None, cu, mx, nbr)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        attn_decode(q, k, v, None, cu, mx, nbr)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ub = unique_bytes(prefix, [suffix] * nbr)
+    print(f"profile case prefix {prefix} x {nbr} branches + {suffix}: {ms:.4f} ms/call, {ub / ms / 1e6:.1f} GB/s "
+          f"unique KV", flush=True)
+    m.check()
 
 
 def _cpu_inputs(m, kids, q, nbranch):
@@ -358,9 +389,13 @@ def main():
     ap.add_argument("--impl", default="mentat", choices=["mentat", "reference"])
     ap.add_argument("--seed", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-case", default=None, metavar="PREFIX,BRANCHES,SUFFIX",
+                    help="time a smaller tree for a profiler capture instead of the benchmark")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_mentat(args)
