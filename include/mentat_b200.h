@@ -35,6 +35,7 @@ extern "C" {
 #define MENTAT_DEV_RELEASE_FREE 3    /* paged_kv_cache.py:63 AssertionError */
 #define MENTAT_DEV_PLAN_OVERFLOW 4   /* decode plan exceeded its workspace */
 #define MENTAT_DEV_TABLE_OVERFLOW 5  /* a sequence outgrew max_blocks_per_seq */
+#define MENTAT_DEV_DECODE_TIMEOUT 6  /* a bounded wait in a decode kernel gave up; that call's output is invalid */
 
 /* dtypes */
 #define MENTAT_F32 0

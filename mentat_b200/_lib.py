@@ -18,6 +18,7 @@ MENTAT_F32, MENTAT_BF16, MENTAT_F16 = 0, 1, 2
 CTRL_HEAD, CTRL_TAIL, CTRL_PEAK, CTRL_ERROR, CTRL_ERRARG, CTRL_ALLOCS, CTRL_COWS = range(7)
 CTRL_WORDS = 16
 DEV_OUT_OF_BLOCKS, DEV_REF_FREE, DEV_RELEASE_FREE, DEV_PLAN_OVERFLOW, DEV_TABLE_OVERFLOW = 1, 2, 3, 4, 5
+DEV_DECODE_TIMEOUT = 6
 GATE_MAXK = 8
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 ERR_SCRATCH_LIMIT = -4

@@ -372,6 +372,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
         ws.hdr[HDR_TC_NEXT] = 0;
         ws.hdr[HDR_NTCN] = s_err ? 0 : totals[KIND_TCN];
         ws.hdr[HDR_TCN_NEXT] = 0;
+        ws.hdr[HDR_TC_ABORT] = 0;
         if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, totals[0] + totals[1] + totals[2]);
     }
     __syncthreads();
@@ -602,7 +603,7 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 // its column over the partials with independent loads.
 constexpr int MERGE_MAXP_SMEM = 1024;
 template <typename T, int D>
-__global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts, T* __restrict__ out,
+__global__ void __launch_bounds__(D) k_merge(mentat_kv_cache c, int Hq, DecodeWs ws, int max_parts, T* __restrict__ out,
                                              int64_t out_stride) {
     constexpr int NW = D / 32;
     constexpr int BATCH = 16;  // independent part loads in flight per thread
@@ -613,6 +614,9 @@ __global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts,
     griddep_launch();
     const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const int P = ws.nparts[i];
+    // a tensor-core unit kernel that gave up a bounded wait left partials unwritten
+    const bool aborted = ws.hdr[HDR_TC_ABORT] != 0;
+    if (aborted && i == 0 && hq == 0 && d == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
     const int64_t pstride = (int64_t)Hq * 2;
     // (m, l) of all partials combined in one reduction: (m1, l1) + (m2, l2) =
@@ -666,7 +670,7 @@ __global__ void __launch_bounds__(D) k_merge(int Hq, DecodeWs ws, int max_parts,
         }
     }
     const float o = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    const float r = (P > 0 && l > 0.f) ? o / l : 0.f;
+    const float r = (P > 0 && l > 0.f && !aborted) ? o / l : 0.f;
     out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
 }
 
@@ -821,7 +825,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
         }
     }
     prof_mark(4, s);
-    if (launch(pdl, k_merge<T, D>, dim3(n, Hq), dim3(D), 0, s, Hq, ws, max_parts, reinterpret_cast<T*>(out),
+    if (launch(pdl, k_merge<T, D>, dim3(n, Hq), dim3(D), 0, s, *c, Hq, ws, max_parts, reinterpret_cast<T*>(out),
                out_stride) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();

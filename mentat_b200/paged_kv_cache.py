@@ -267,6 +267,9 @@ class PagedKVCacheManager:
                                f"max_blocks_per_seq={self.max_blocks_per_seq})")
         if err == _lib.DEV_PLAN_OVERFLOW:
             raise RuntimeError("mentat_b200: decode plan workspace overflow")
+        if err == _lib.DEV_DECODE_TIMEOUT:
+            raise RuntimeError(f"mentat_b200: a decode kernel's bounded wait gave up (stage {arg}); "
+                               "that call's output is invalid")
         raise RuntimeError(f"mentat_b200 device error {err} ({arg})")
 
     def _after(self):
