@@ -603,73 +603,91 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 // its column over the partials with independent loads.
 constexpr int MERGE_MAXP_SMEM = 1024;
 template <typename T, int D>
-__global__ void __launch_bounds__(D) k_merge(mentat_kv_cache c, int Hq, DecodeWs ws, int max_parts, T* __restrict__ out,
-                                             int64_t out_stride) {
+__global__ void __launch_bounds__(D, 2048 / D) k_merge(mentat_kv_cache c, int Hq, DecodeWs ws, int max_parts,
+                                                       T* __restrict__ out, int64_t out_stride) {
     constexpr int NW = D / 32;
-    constexpr int BATCH = 16;  // independent part loads in flight per thread
+    constexpr int B = 8;  // partial rows loaded per batch
     __shared__ float s_w[MERGE_MAXP_SMEM];
     __shared__ float s_rm[NW], s_rl[NW];
     __shared__ float s_ml[2];
     griddep_wait();  // every unit kernel's partials
     griddep_launch();
     const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
+    const int64_t pstride = (int64_t)Hq * 2;
+    const float* po = ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + d;
+    const int64_t ostride = (int64_t)Hq * D;
+    // the first batch of partial rows is loaded before the part count is known:
+    // rows up to max_parts exist in the workspace, and those past the count are
+    // masked below (their contents are never used)
+    float v[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) v[j] = j < max_parts ? po[j * ostride] : 0.f;
     const int P = ws.nparts[i];
     // a tensor-core unit kernel that gave up a bounded wait left partials unwritten
     const bool aborted = ws.hdr[HDR_TC_ABORT] != 0;
     if (aborted && i == 0 && hq == 0 && d == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
-    const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
-    const int64_t pstride = (int64_t)Hq * 2;
-    // (m, l) of all partials combined in one reduction: (m1, l1) + (m2, l2) =
-    // (M, l1 2^(m1 - M) + l2 2^(m2 - M)), M = max(m1, m2)
-    float m = -INFINITY, l = 0.f;
-    for (int p = d; p < P; p += D) {
-        const float2 v = *reinterpret_cast<const float2*>(ml + p * pstride);
-        const float mn = fmaxf(m, v.x);
-        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (v.x == -INFINITY ? 0.f : v.y * exp2f(v.x - mn));
-        m = mn;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+    // (m, l) of all partials combined: (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
+    auto comb = [](float& m, float& l, float m2, float l2) {
         const float mn = fmaxf(m, m2);
         l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (m2 == -INFINITY ? 0.f : l2 * exp2f(m2 - mn));
         m = mn;
-    }
-    if (lane == 0) {
-        s_rm[warp] = m;
-        s_rl[warp] = l;
-    }
-    __syncthreads();
-    if (d == 0) {
-        float mm = s_rm[0], ll = s_rl[0];
-        for (int w2 = 1; w2 < NW; ++w2) {
-            const float m2 = s_rm[w2], l2 = s_rl[w2];
-            const float mn = fmaxf(mm, m2);
-            ll = (mm == -INFINITY ? 0.f : ll * exp2f(mm - mn)) + (m2 == -INFINITY ? 0.f : l2 * exp2f(m2 - mn));
-            mm = mn;
-        }
-        s_ml[0] = mm;
-        s_ml[1] = ll;
-    }
-    __syncthreads();
-    m = s_ml[0];
-    l = s_ml[1];
-    for (int p = d; p < P && p < MERGE_MAXP_SMEM; p += D) s_w[p] = exp2f(ml[p * pstride] - m);
-    __syncthreads();
-    const float* po = ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + d;
-    const int64_t ostride = (int64_t)Hq * D;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int p0 = 0; p0 < P; p0 += BATCH) {
-        float v[BATCH];
+    };
+    if (P <= 32) {  // one warp
+        if (warp == 0) {
+            float m = -INFINITY, l = 0.f;
+            if (lane < P) {
+                const float2 x = *reinterpret_cast<const float2*>(ml + lane * pstride);
+                m = x.x;
+                l = x.y;
+            }
+            const float mp = m;
 #pragma unroll
-        for (int j = 0; j < BATCH; ++j) v[j] = p0 + j < P ? po[(p0 + j) * ostride] : 0.f;
-#pragma unroll
-        for (int j = 0; j < BATCH; ++j) {
-            const int p = p0 + j;
-            if (p < P) acc[j & 3] += v[j] * (p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m));
+            for (int o = 16; o; o >>= 1) comb(m, l, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, l, o));
+            if (lane < P) s_w[lane] = exp2f(mp - m);
+            if (lane == 0) {
+                s_ml[0] = m;
+                s_ml[1] = l;
+            }
         }
+    } else {
+        float m = -INFINITY, l = 0.f;
+        for (int p = d; p < P; p += D) {
+            const float2 x = *reinterpret_cast<const float2*>(ml + p * pstride);
+            comb(m, l, x.x, x.y);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) comb(m, l, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, l, o));
+        if (lane == 0) {
+            s_rm[warp] = m;
+            s_rl[warp] = l;
+        }
+        __syncthreads();
+        if (d == 0) {
+            float mm = s_rm[0], ll = s_rl[0];
+            for (int w2 = 1; w2 < NW; ++w2) comb(mm, ll, s_rm[w2], s_rl[w2]);
+            s_ml[0] = mm;
+            s_ml[1] = ll;
+        }
+        __syncthreads();
+        const float mm = s_ml[0];
+        for (int p = d; p < P && p < MERGE_MAXP_SMEM; p += D) s_w[p] = exp2f(ml[p * pstride] - mm);
     }
-    const float o = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    __syncthreads();
+    const float m = s_ml[0], l = s_ml[1];
+    auto weight = [&](int p) { return p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m); };
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < B; ++j)
+        if (j < P) (j & 1 ? acc1 : acc0) += v[j] * weight(j);
+    for (int p0 = B; p0 < P; p0 += B) {
+#pragma unroll
+        for (int j = 0; j < B; ++j) v[j] = p0 + j < P ? po[(p0 + j) * ostride] : 0.f;
+#pragma unroll
+        for (int j = 0; j < B; ++j)
+            if (p0 + j < P) (j & 1 ? acc1 : acc0) += v[j] * weight(p0 + j);
+    }
+    const float o = acc0 + acc1;
     const float r = (P > 0 && l > 0.f && !aborted) ? o / l : 0.f;
     out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
 }

@@ -244,6 +244,9 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                 break;
             }
             TCN_TRACE(0);
+#ifdef MENTAT_TC_TRACE
+            if (blockIdx.x == 0 && tid == 0 && k < 64) g_tc_trace[3072 + 4 * k] = clock64();
+#endif
             const int* su = s_unit[slot];
             const int q_lo = su[0], q_hi = su[1], t0u = su[2], t1u = su[3], ord = su[4], head = su[5];
             const int R = (q_hi - q_lo + 1) * G;
@@ -288,6 +291,9 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                         if (!mbar_wait(bar_s0 + 8 * (g & 1), (g >> 1) & 1)) s_abort = 1;
                         tc_fence_after();
                         TCN_TRACE(10 + 8 * i);
+#ifdef MENTAT_TC_TRACE
+                        if (blockIdx.x == 0 && tid == 0 && i == 0 && k < 64) g_tc_trace[3072 + 4 * k + 1] = clock64();
+#endif
                         float sv[NR];
                         tmem_ld_n<NR>(tmem + lane_off + 32 + 32 * (g & 1), sv);
                         const int t = (blk0 + 8 * i) * 16 + tid;  // this thread's token
@@ -432,6 +438,10 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
             TCN_TRACE(4);
 #ifdef MENTAT_TC_TRACE
             g_trace_on = false;
+            if (blockIdx.x == 0 && tid == 0 && k < 64) {
+                g_tc_trace[3072 + 4 * k + 2] = clock64();
+                g_tc_trace[3072 + 4 * k + 3] = ntiles;
+            }
 #endif
             g0 += ntiles;
             // unit done: O^T, S^T and the slot's Q may be reused
