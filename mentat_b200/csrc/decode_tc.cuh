@@ -569,10 +569,9 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
             if (rows_live) {
                 const int tb = (blk0 + BPT * i) * 16;  // first token of the tile
                 const bool full = tb >= t0u && tb + TC_TILE <= t1u;
-                // scaled, masked score of token j of the tile
-                auto score = [&](float x, int j) {
-                    return (full || (tb + j >= t0u && tb + j < t1u)) ? x * scale_log2 : -INFINITY;
-                };
+                // the row max is taken on raw scores (scale > 0 keeps the order) and the
+                // scale is folded into the exponent's argument: p = 2^(s*scale - m_ref)
+                auto valid = [&](int j) { return full || (tb + j >= t0u && tb + j < t1u); };
                 // tokens 64-127 stay in registers; tokens 0-63 are read for the max
                 // here and again, 32 at a time, for their probabilities
                 float hi[64];
@@ -581,16 +580,16 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     float lo[64];
                     tmem_ld64(s_col, lo);
 #pragma unroll
-                    for (int j = 0; j < 64; ++j) mx = fmaxf(mx, score(lo[j], j));
+                    for (int j = 0; j < 64; ++j) mx = fmaxf(mx, valid(j) ? lo[j] : -INFINITY);
                 }
                 tmem_ld64(s_col + 64, hi);
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
-                    hi[j] = score(hi[j], 64 + j);
+                    if (!valid(64 + j)) hi[j] = -INFINITY;
                     mx = fmaxf(mx, hi[j]);
                 }
                 float fac = 1.f;
-                const float m_new = fmaxf(m_ref, mx);
+                const float m_new = fmaxf(m_ref, mx * scale_log2);
                 if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
                     if (m_ref != -INFINITY) {
                         fac = ex2_approx(m_ref - m_new);
@@ -598,6 +597,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     }
                     m_ref = m_new;
                 }
+                const float neg_m = -m_ref;
                 // rows whose reference max rose rescale O; S(i) being complete means
                 // P V(i-1) of this row tile is complete too (issued before S(i))
                 if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
@@ -622,8 +622,9 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const float a = ex2_approx(score(v[2 * e], 32 * cchunk + 2 * e) - m_ref);
-                        const float b = ex2_approx(score(v[2 * e + 1], 32 * cchunk + 2 * e + 1) - m_ref);
+                        const int j = 32 * cchunk + 2 * e;
+                        const float a = valid(j) ? ex2_approx(fmaf(v[2 * e], scale_log2, neg_m)) : 0.f;
+                        const float b = valid(j + 1) ? ex2_approx(fmaf(v[2 * e + 1], scale_log2, neg_m)) : 0.f;
                         acc += a + b;
                         pk[e] = Pair<T>::pack(a, b);
                     }
@@ -634,8 +635,8 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const float a = ex2_approx(hi[32 * cchunk + 2 * e] - m_ref);
-                        const float b = ex2_approx(hi[32 * cchunk + 2 * e + 1] - m_ref);
+                        const float a = ex2_approx(fmaf(hi[32 * cchunk + 2 * e], scale_log2, neg_m));
+                        const float b = ex2_approx(fmaf(hi[32 * cchunk + 2 * e + 1], scale_log2, neg_m));
                         acc += a + b;
                         pk[e] = Pair<T>::pack(a, b);
                     }
