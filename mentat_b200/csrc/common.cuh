@@ -35,6 +35,25 @@ namespace mentat {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// device timeline of one call (trace builds only): nanosecond stamps, first and
+// last over the CTAs of a kernel
+#ifdef MENTAT_TC_TRACE
+static __device__ unsigned long long g_timeline[32];
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+static __device__ unsigned long long g_cta_end[2][256];  // per CTA of the wide (0) and narrow (1) kernel
+#define TL_CTA_END(w) do { if (threadIdx.x == 0 && blockIdx.x < 256) mentat::g_cta_end[(w)][blockIdx.x] = mentat::gtime(); } while (0)
+#define TL_FIRST(k) do { if (threadIdx.x == 0) atomicMin(&mentat::g_timeline[(k)], mentat::gtime()); } while (0)
+#define TL_LAST(k) do { if (threadIdx.x == 0) atomicMax(&mentat::g_timeline[(k)], mentat::gtime()); } while (0)
+#else
+#define TL_FIRST(k) do { } while (0)
+#define TL_LAST(k) do { } while (0)
+#define TL_CTA_END(w) do { } while (0)
+#endif
+
 // ---------------------------------------------------------------------------
 // element types
 // ---------------------------------------------------------------------------

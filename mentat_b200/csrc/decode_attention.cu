@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(LCP_THREADS) k_lcp(mentat_kv_cache c, int laye
     __shared__ int s_min[LCP_THREADS / 32];
     griddep_wait();  // tables and lengths may come from the previous launch on the stream
     griddep_launch();
+    TL_FIRST(0);
     const int pair = blockIdx.x + 1;  // compares sequences pair-1 and pair
     if (pair >= n) return;
     int sa = slots[pair - 1], sb = slots[pair];
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(LCP_THREADS) k_lcp(mentat_kv_cache c, int laye
         __syncthreads();
     }
     if (threadIdx.x == 0) ws.lcp[pair] = first;
+    TL_LAST(1);
 }
 
 // Plan parameters for one launch.  A segment (node of the LCP-interval tree or
@@ -181,16 +183,20 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __shared__ int s_nnodes, s_err;
     const int tid = threadIdx.x;
     const int bs = c.block_size;
-    griddep_wait();  // the pair LCPs
-    griddep_launch();
-    PLAN_TRACE(0);
-
+    // With the LCP kernel ahead of this one (n > 1), the slots and lengths were
+    // final when that kernel passed its own wait, so they are read while it runs;
+    // otherwise they may come from the previous launch and are read after the wait.
+    if (n <= 1) griddep_wait();
     for (int i = tid; i < n; i += blockDim.x) {
         int slot = slots[i];
         if (slot < 0 || slot >= c.max_seqs) slot = 0;
         s_slot[i] = slot;
         s_len[i] = c.ntok[seq_index(c, layer, slot)];
     }
+    if (n > 1) griddep_wait();  // the pair LCPs
+    griddep_launch();
+    TL_FIRST(2);
+    PLAN_TRACE(0);
     if (tid == 0) {
         s_h[0] = 0;
         s_h[n] = 0;
@@ -466,6 +472,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     }
     __syncthreads();
     PLAN_TRACE(6);
+    TL_LAST(3);
 }
 
 // ---------------------------------------------------------------------------
@@ -606,12 +613,13 @@ template <typename T, int D>
 __global__ void __launch_bounds__(D, 2048 / D) k_merge(mentat_kv_cache c, int Hq, DecodeWs ws, int max_parts,
                                                        T* __restrict__ out, int64_t out_stride) {
     constexpr int NW = D / 32;
-    constexpr int B = 8;  // partial rows loaded per batch
+    constexpr int B = 12;  // partial rows loaded per batch
     __shared__ float s_w[MERGE_MAXP_SMEM];
     __shared__ float s_rm[NW], s_rl[NW];
     __shared__ float s_ml[2];
     griddep_wait();  // every unit kernel's partials
     griddep_launch();
+    TL_FIRST(8);
     const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
     const int64_t pstride = (int64_t)Hq * 2;
@@ -690,6 +698,7 @@ __global__ void __launch_bounds__(D, 2048 / D) k_merge(mentat_kv_cache c, int Hq
     const float o = acc0 + acc1;
     const float r = (P > 0 && l > 0.f && !aborted) ? o / l : 0.f;
     out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
+    TL_LAST(9);
 }
 
 }  // namespace mentat
@@ -964,6 +973,17 @@ extern "C" int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t lay
 #ifdef MENTAT_TC_TRACE
 extern "C" int mentat_plan_trace_dump(long long* host) {
     return cudaMemcpyFromSymbol(host, g_plan_trace, sizeof(long long) * 16) == cudaSuccess ? 0 : -2;
+}
+extern "C" int mentat_timeline_reset() {
+    unsigned long long init[32];
+    for (int k = 0; k < 32; ++k) init[k] = (k % 2 == 0) ? ~0ull : 0ull;  // even: first (min), odd: last (max)
+    return cudaMemcpyToSymbol(mentat::g_timeline, init, sizeof(init)) == cudaSuccess ? 0 : -2;
+}
+extern "C" int mentat_timeline_dump(unsigned long long* host) {
+    return cudaMemcpyFromSymbol(host, mentat::g_timeline, sizeof(unsigned long long) * 32) == cudaSuccess ? 0 : -2;
+}
+extern "C" int mentat_cta_end_dump(unsigned long long* host) {
+    return cudaMemcpyFromSymbol(host, mentat::g_cta_end, sizeof(unsigned long long) * 512) == cudaSuccess ? 0 : -2;
 }
 extern "C" int mentat_tc_trace_dump(long long* host, int n) {
     return cudaMemcpyFromSymbol(host, mentat::g_tc_trace, sizeof(long long) * (n < 4096 ? n : 4096)) == cudaSuccess ? 0 : -2;

@@ -384,6 +384,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     // narrow kernel after this one may start on the SMs this one leaves free.
     griddep_wait();
     griddep_launch();
+    TL_FIRST(4);
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
 #endif
@@ -712,6 +713,8 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     if (warp == 0) tmem_dealloc(tmem, TC_TMEM_COLS);
+    TL_LAST(5);
+    TL_CTA_END(0);
 }
 
 // ---------------------------------------------------------------------------

@@ -132,6 +132,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     // the wide one until its end, so the two overlap on the SMs the wide kernel
     // leaves free.
     griddep_launch();
+    TL_FIRST(6);
 
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
@@ -463,6 +464,8 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     if (warp == 0) tmem_dealloc(tmem, TCN_TMEM_COLS);
+    TL_LAST(7);
+    TL_CTA_END(1);
     griddep_wait();  // complete only after the wide kernel: the merge reads both kernels' partials
 }
 
