@@ -16,11 +16,11 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
-from . import _lib
+from . import ops
 from .paged_kv_cache import PagedKV
 
 BACKEND = "mentat_b200"
-MAX_SEQS_PER_LAUNCH = 512
+MAX_SEQS_PER_LAUNCH = ops.MAX_SEQS_PER_LAUNCH
 
 
 def attn_decode(q: torch.Tensor, k, v, cu_seqlens_q: torch.Tensor = None, cu_seqlens_k: torch.Tensor = None,
@@ -48,20 +48,10 @@ def attn_decode(q: torch.Tensor, k, v, cu_seqlens_q: torch.Tensor = None, cu_seq
         raise TypeError(f"q dtype {q.dtype} differs from the cache dtype {mgr.dtype}")
     if q.stride(2) != 1 or q.stride(1) != d:
         q = q.contiguous()
-    out = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
     if n == 0:
-        return out
+        return torch.empty((0, hq, d), device=q.device, dtype=q.dtype)
     scale = 1.0 / math.sqrt(d) if softmax_scale is None else float(softmax_scale)
-    lib = _lib.load()
-    stream = torch.cuda.current_stream(q.device).cuda_stream
-    for a in range(0, n, MAX_SEQS_PER_LAUNCH):
-        b = min(n, a + MAX_SEQS_PER_LAUNCH)
-        ws, wsb, parts = mgr.decode_workspace(b - a, hq, max(k.lens[a:b]))
-        _lib.check(lib.mentat_paged_decode(
-            mgr._descp, k.layer, k.slots.data_ptr() + 4 * a, b - a,
-            q.data_ptr() + a * q.stride(0) * q.element_size(), q.stride(0), hq,
-            out.data_ptr() + a * out.stride(0) * out.element_size(), out.stride(0), scale,
-            ws.data_ptr(), wsb, parts, stream), "mentat_paged_decode")
+    out = torch.ops.mentat_b200.paged_decode(q[:n], k.slots, max(k.lens), mgr._op_id, k.layer, scale)
     if mgr.strict:
         mgr.check()
     return out

@@ -20,7 +20,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, ops  # noqa: F401  (ops registers torch.ops.mentat_b200.gate_step)
 
 _DT = {torch.bfloat16: _lib.MENTAT_BF16, torch.float16: _lib.MENTAT_F16, torch.float32: _lib.MENTAT_F32}
 
@@ -90,15 +90,13 @@ class Gate:
             self._hist_dev[:nh].copy_(self._hist_host[:nh], non_blocking=True)
         self._ema_dev[:n].copy_(self._ema_host[:n], non_blocking=True)
         c = self.cfg
-        p = _lib.GateParams(c.temperature, c.repetition_penalty, c.entropy_ema_alpha, c.relative_entropy_multiplier,
-                            c.soft_explore_initial, c.branching_factor, c.max_active_branches, num_active, step,
-                            c.soft_explore_window, 0)
-        s = torch.cuda.current_stream(self.device).cuda_stream
-        _lib.check(self.lib.mentat_gate_step(
-            logits.data_ptr(), _DT[logits.dtype], n, V, logits.stride(0), self._ptr_dev.data_ptr(),
-            self._hist_dev.data_ptr(), self._ema_dev.data_ptr(), C.byref(p), self._out_dev.data_ptr(), s),
-            "mentat_gate_step")
         nb = n * GATE_OUT_DTYPE.itemsize
+        torch.ops.mentat_b200.gate_step(
+            logits, self._ptr_dev[: n + 1], self._hist_dev, self._ema_dev[:n],
+            [c.temperature, c.repetition_penalty, c.entropy_ema_alpha, c.relative_entropy_multiplier,
+             c.soft_explore_initial],
+            [c.branching_factor, c.max_active_branches, num_active, step, c.soft_explore_window],
+            self._out_dev[:nb])
         self._out_host[:nb].copy_(self._out_dev[:nb], non_blocking=True)
         self._n = n
 

@@ -1,0 +1,122 @@
+"""torch custom operators over the C ABI (``torch.library``).
+
+The public Python API (``PagedKVCacheManager.append_tokens_batched``,
+``attention_backend.attn_decode``, ``gate.Gate``) reaches the library through
+these operators, so the three hot-path calls are visible to torch as ops with
+schemas and fake (meta) implementations: torch.compile can trace a caller that
+uses them and CUDA-graph capture sees ordinary op calls.  Each operator
+launches on the current torch stream and returns without synchronising.
+
+A cache is passed as the integer id it registered under (``register_cache``),
+because operator arguments are tensors and scalars.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import itertools
+import math
+import weakref
+
+import torch
+
+from . import _lib
+
+_caches: "weakref.WeakValueDictionary[int, object]" = weakref.WeakValueDictionary()
+_ids = itertools.count(1)
+
+MAX_SEQS_PER_LAUNCH = 512  # mentat_paged_decode's per-launch sequence limit
+
+
+def register_cache(mgr) -> int:
+    """Registers a ``PagedKVCacheManager``; returns the id the operators take."""
+    i = next(_ids)
+    _caches[i] = mgr
+    return i
+
+
+def _cache(i: int):
+    mgr = _caches.get(i)
+    if mgr is None:
+        raise RuntimeError(f"mentat_b200: no live cache with id {i}")
+    return mgr
+
+
+@torch.library.custom_op("mentat_b200::paged_decode", mutates_args=(), device_types="cuda")
+def paged_decode(q: torch.Tensor, slots: torch.Tensor, max_len: int, cache: int, layer: int,
+                 scale: float) -> torch.Tensor:
+    """Tree-aware decode attention of ``q`` (N, Hq, D) over the cached sequences in
+    ``slots`` (N,) int32 of layer ``layer``; ``max_len`` is the longest of their
+    lengths (it sizes the workspace).  Wraps ``mentat_paged_decode``."""
+    mgr = _cache(cache)
+    lib = _lib.load()
+    n, hq, d = q.shape
+    out = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    for a in range(0, n, MAX_SEQS_PER_LAUNCH):
+        b = min(n, a + MAX_SEQS_PER_LAUNCH)
+        ws, wsb, parts = mgr.decode_workspace(b - a, hq, max_len)
+        _lib.check(lib.mentat_paged_decode(
+            mgr._descp, layer, slots.data_ptr() + 4 * a, b - a,
+            q.data_ptr() + a * q.stride(0) * q.element_size(), q.stride(0), hq,
+            out.data_ptr() + a * out.stride(0) * out.element_size(), out.stride(0), scale,
+            ws.data_ptr(), wsb, parts, stream), "mentat_paged_decode")
+    return out
+
+
+@paged_decode.register_fake
+def _paged_decode_fake(q, slots, max_len, cache, layer, scale):
+    return torch.empty_like(q)
+
+
+@torch.library.custom_op("mentat_b200::append_batched", mutates_args=("k_pool", "v_pool"), device_types="cuda")
+def append_batched(k_pool: torch.Tensor, v_pool: torch.Tensor, slots: torch.Tensor, k: torch.Tensor,
+                   v: torch.Tensor, cache: int, layer: int) -> None:
+    """Appends one token per sequence (rows of ``k``, ``v``: (N, Hkv, D)) to the
+    sequences in ``slots`` of layer ``layer``, allocating and copying-on-write on
+    the device.  ``k_pool`` / ``v_pool`` are the cache's pools, named so that
+    torch knows what the operator writes.  Wraps ``mentat_kv_append_batched``."""
+    mgr = _cache(cache)
+    lib = _lib.load()
+    n = k.shape[0]
+    ks, vs = k.stride(0), v.stride(0)
+    stream = torch.cuda.current_stream(k.device).cuda_stream
+    for a in range(0, n, 1024):
+        b = min(n, a + 1024)
+        _lib.check(lib.mentat_kv_append_batched(
+            mgr._descp, layer, slots.data_ptr() + 4 * a, b - a,
+            k.data_ptr() + a * ks * k.element_size(), ks,
+            v.data_ptr() + a * vs * v.element_size(), vs, stream), "append_tokens_batched")
+
+
+@append_batched.register_fake
+def _append_batched_fake(k_pool, v_pool, slots, k, v, cache, layer):
+    return None
+
+
+@torch.library.custom_op("mentat_b200::gate_step", mutates_args=("out",), device_types="cuda")
+def gate_step(logits: torch.Tensor, hist_ptr: torch.Tensor, hist_ids: torch.Tensor, ema_old: torch.Tensor,
+              params: list[float], ints: list[int], out: torch.Tensor) -> None:
+    """The fused entropy gate over ``logits`` (N, V) into ``out`` (N records of
+    ``mentat_gate_out`` as bytes).  ``params`` = (temperature, penalty, alpha,
+    multiplier, soft-explore initial), ``ints`` = (K, max_active, num_active,
+    step, soft-explore window).  Wraps ``mentat_gate_step``."""
+    lib = _lib.load()
+    n, V = logits.shape
+    p = _lib.GateParams(*params, *ints, 0)
+    stream = torch.cuda.current_stream(logits.device).cuda_stream
+    _lib.check(lib.mentat_gate_step(
+        logits.data_ptr(), _DT[logits.dtype], n, V, logits.stride(0), hist_ptr.data_ptr(), hist_ids.data_ptr(),
+        ema_old.data_ptr(), C.byref(p), out.data_ptr(), stream), "mentat_gate_step")
+
+
+@gate_step.register_fake
+def _gate_step_fake(logits, hist_ptr, hist_ids, ema_old, params, ints, out):
+    return None
+
+
+_DT = {torch.bfloat16: _lib.MENTAT_BF16, torch.float16: _lib.MENTAT_F16, torch.float32: _lib.MENTAT_F32}
+
+
+def default_scale(d: int) -> float:
+    return 1.0 / math.sqrt(d)

@@ -29,7 +29,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import _lib
+from . import _lib, ops
 
 _DTYPES = {torch.float32: _lib.MENTAT_F32, torch.bfloat16: _lib.MENTAT_BF16, torch.float16: _lib.MENTAT_F16}
 
@@ -239,6 +239,7 @@ class PagedKVCacheManager:
         self._cache: dict = {}
         self._ws = None
         self._uploads = _PinnedRing(self.device)
+        self._op_id = ops.register_cache(self)
         self._ws_bytes = 0
 
     # ------------------------------------------------------------------ util
@@ -381,12 +382,7 @@ class PagedKVCacheManager:
         for s in seqs:
             self._mirror_append(s, layer_idx, 1)
         slots = self._slots_dev(seq_ids)
-        for a in range(0, N, 1024):
-            b = min(N, a + 1024)
-            _lib.check(self._lib.mentat_kv_append_batched(
-                self._descp, layer_idx, slots.data_ptr() + 4 * a, b - a,
-                k.data_ptr() + a * ks * k.element_size(), ks,
-                v.data_ptr() + a * vs * v.element_size(), vs, self._s()), "append_tokens_batched")
+        torch.ops.mentat_b200.append_batched(self._k_all, self._v_all, slots, k, v, self._op_id, layer_idx)
         self._after()
 
     def get_kv_length(self, seq_id: int) -> int:            # :285-287
