@@ -46,6 +46,23 @@ def _env_rank():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def combine_ranks(ms, e2e_ms, kv_bytes, e2e_bytes, device, world):
+    """Whole-job GB/s of the device-timed loop and of the end-to-end loop.
+
+    Every rank decodes its own tree, so the job moves the sum of the ranks'
+    bytes in the time of the slowest rank (max over ranks of its device time).
+    Returns (value, e2e value, slowest device time in ms)."""
+    import torch.distributed as dist
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=device)
+    tot = torch.tensor([float(kv_bytes), float(e2e_bytes)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms_max, e2e_max = t.tolist()
+    kv_all, e2e_all = tot.tolist()
+    return kv_all / (ms_max / 1e3) / 1e9, e2e_all / (e2e_max / 1e3) / 1e9, ms_max
+
+
 def suffixes(seed):
     return np.random.default_rng(seed).integers(SUF_LO, SUF_HI + 1, NBR)
 
@@ -315,15 +332,7 @@ def run_mentat(args):
     e2e_ms = a0.elapsed_time(a1)
     m.check()
 
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=device)
-    tot = torch.tensor([float(ub), float(e2e_bytes)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-    ms_max, e2e_max = t.tolist()
-    ub_all, e2e_all = tot.tolist()
-    value = ub_all * args.steps / (ms_max / 1e3) / 1e9
-    e2e_val = e2e_all / (e2e_max / 1e3) / 1e9
+    value, e2e_val, ms_max = combine_ranks(ms, e2e_ms, ub * args.steps, e2e_bytes, device, world)
     n_prof = max(cnt.value, 1)
     st_ms = {"plan": stage[0] / n_prof, "units_ffma": stage[1] / n_prof, "units_tc": stage[2] / n_prof,
              "units_tcn": stage[3] / n_prof, "merge": stage[4] / n_prof}
