@@ -1,0 +1,356 @@
+"""Entropy-gated prefix-tree rollout on the B200 decode path.
+
+This runs the algorithm of the reference's ``MentatGenerator.generate``
+(``core/generator.py:124-245``) with this package's pieces on the hot path:
+
+* the paged cache (``PagedKVCacheManager``: device allocator, fork, batched
+  append with copy-on-write),
+* tree-aware decode attention (``attn_decode``: shared prefixes read once),
+* the fused gate (``Gate``: entropy, EMA, threshold, repetition penalty and the
+  branch / extend decision of every active leaf in one launch and one
+  device-to-host read per step, where the reference runs per-leaf Python with
+  several host synchronisations, ``generator.py:333-374``).
+
+The model stays a Hugging Face causal LM (Qwen3 or Llama family); ``PagedLM``
+drives its layers the way the reference's ``PagedModelWrapper`` and adapters
+do (``generator_utils.py:255-418``, ``adapters/qwen3_adapter.py``,
+``adapters/llama_adapter.py``): pre-attention norm, q/k/v projections, QK-norm
+on Qwen3, rotate-half RoPE at the sequence's cached length, append, attention,
+o_proj, MLP, final norm and lm_head.
+
+``TreeRollout.generate_many`` runs several trees in lockstep, one batched
+forward pass per step for the active leaves of all of them (the reference
+handles one tree per ``generate``); each tree keeps its own gate state and
+decisions, so every tree's result is what ``generate`` alone would give.
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from .attention_backend import attn_decode, attn_prefill
+from .gate import Gate, GateConfig
+from .paged_kv_cache import PagedKVCacheManager
+
+
+# ---------------------------------------------------------------------------
+# tree (generator_utils.py:40-189)
+# ---------------------------------------------------------------------------
+@dataclass(eq=False)
+class Node:
+    node_id: int
+    token_ids: list = field(default_factory=list)
+    seq_id: Optional[int] = None
+    parent: Optional["Node"] = None
+    children: dict = field(default_factory=dict)
+    cumulative_log_prob: float = 0.0
+    depth: int = 0
+    is_active: bool = True
+    is_eos: bool = False
+    semantic_vector: Optional[torch.Tensor] = None
+    entropy_ema: Optional[float] = None
+    creation_step: int = 0
+    is_pruned: bool = False
+
+    def full_sequence(self) -> list:
+        """Generated token ids from the root to this node (the prompt is not part)."""
+        parts, node = [], self
+        while node is not None:
+            if node.token_ids:
+                parts.append(node.token_ids)
+            node = node.parent
+        return [t for seg in reversed(parts) for t in seg]
+
+
+class Tree:
+    """Branches of one rollout, each live leaf backed by a cache sequence."""
+
+    def __init__(self, cache: PagedKVCacheManager):
+        self.root = Node(node_id=0)
+        self.cache = cache
+        self._next = 1
+
+    def new_id(self) -> int:
+        i, self._next = self._next, self._next + 1
+        return i
+
+    def extend(self, leaf: Node, token: int, log_prob: float) -> None:        # :89-99
+        leaf.token_ids.append(token)
+        leaf.cumulative_log_prob += log_prob
+        leaf.depth += 1
+
+    def branch(self, leaf: Node, tokens, log_probs) -> list:                   # :102-138
+        kids = []
+        for t, lp in zip(tokens, log_probs):
+            child = Node(node_id=self.new_id(), token_ids=[int(t)], seq_id=self.cache.fork_sequence(leaf.seq_id),
+                         parent=leaf, cumulative_log_prob=leaf.cumulative_log_prob + float(lp), depth=leaf.depth + 1,
+                         entropy_ema=leaf.entropy_ema,
+                         semantic_vector=None if leaf.semantic_vector is None else leaf.semantic_vector.clone())
+            leaf.children[child.node_id] = child
+            kids.append(child)
+        leaf.is_active = False
+        if leaf.seq_id is not None:
+            self.cache.free_sequence(leaf.seq_id)
+            leaf.seq_id = None
+        return kids
+
+    def prune(self, node: Node) -> None:                                       # :141-169
+        if node.seq_id is not None:
+            self.cache.free_sequence(node.seq_id)
+            node.seq_id = None
+        node.is_active = False
+        node.is_pruned = True
+        p = node.parent
+        if p is not None and not p.is_active and p.parent is not None and \
+                all(c.is_pruned for c in p.children.values()):
+            self.prune(p)
+
+    def active_leaves(self) -> list:                                           # :171-189
+        out = []
+        self._walk(self.root, out, True)
+        return out
+
+    def finished(self) -> list:
+        out = []
+        self._walk(self.root, out, False)
+        return out
+
+    def _walk(self, node: Node, out: list, active: bool) -> None:
+        if active:
+            if node.is_active and not node.children and not node.is_eos:
+                out.append(node)
+        elif node.is_eos:
+            out.append(node)
+        for c in node.children.values():
+            self._walk(c, out, active)
+
+    def free_all(self) -> None:
+        stack = [self.root]
+        while stack:
+            n = stack.pop()
+            if n.seq_id is not None:
+                self.cache.free_sequence(n.seq_id)
+                n.seq_id = None
+            stack.extend(n.children.values())
+
+
+# ---------------------------------------------------------------------------
+# model driver (generator_utils.py:255-418, adapters/*_adapter.py)
+# ---------------------------------------------------------------------------
+class PagedLM:
+    """Runs a Hugging Face Qwen3 / Llama causal LM over the paged cache."""
+
+    def __init__(self, model, cache: PagedKVCacheManager):
+        base = model.model
+        self.model, self.cache = model, cache
+        self.embed, self.layers, self.norm, self.lm_head = base.embed_tokens, base.layers, base.norm, model.lm_head
+        self.rotary = base.rotary_emb
+        cfg = model.config
+        self.hq, self.hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.hq
+        self.qk_norm = hasattr(self.layers[0].self_attn, "q_norm")  # Qwen3
+
+    @staticmethod
+    def _rope(t, cos, sin):
+        h = t.shape[-1] // 2
+        return t * cos + torch.cat((-t[..., h:], t[..., :h]), dim=-1) * sin
+
+    def _qkv(self, attn, x, shape):
+        q = attn.q_proj(x).view(*shape, self.hq, self.hd)
+        k = attn.k_proj(x).view(*shape, self.hkv, self.hd)
+        v = attn.v_proj(x).view(*shape, self.hkv, self.hd)
+        if self.qk_norm:
+            q, k = attn.q_norm(q), attn.k_norm(k)
+        return q, k, v
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor, seq_id: int) -> torch.Tensor:
+        """The prompt (L,) into the cache of ``seq_id``; logits (V,) of its last position."""
+        L = input_ids.shape[-1]
+        h = self.embed(input_ids.view(1, L))
+        pos = torch.arange(L, device=h.device).view(1, L)
+        cos, sin = self.rotary(h, pos)
+        cos, sin = cos.unsqueeze(2), sin.unsqueeze(2)  # (1, L, 1, hd)
+        for layer_idx, blk in enumerate(self.layers):
+            attn = blk.self_attn
+            q, k, v = self._qkv(attn, blk.input_layernorm(h), (1, L))
+            q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
+            o = attn_prefill(q, k, v)
+            self.cache.append_tokens(seq_id, layer_idx, k[0], v[0])
+            h = h + attn.o_proj(o.reshape(1, L, -1))
+            h = h + blk.mlp(blk.post_attention_layernorm(h))
+        return self.lm_head(self.norm(h)[0, -1])
+
+    @torch.no_grad()
+    def decode(self, tokens: torch.Tensor, seq_ids: list) -> tuple:
+        """One token per sequence: logits (N, V) and final hidden states (N, D)."""
+        N = len(seq_ids)
+        h = self.embed(tokens.view(N))
+        pos = torch.tensor([self.cache.get_kv_length(s) for s in seq_ids], device=h.device).view(N, 1)
+        cos, sin = self.rotary(h, pos)  # (N, 1, hd): broadcasts over heads
+        for layer_idx, blk in enumerate(self.layers):
+            attn = blk.self_attn
+            q, k, v = self._qkv(attn, blk.input_layernorm(h), (N,))
+            q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
+            # the new token's K/V go in first, so it attends to itself
+            self.cache.append_tokens_batched(seq_ids, layer_idx, k, v)
+            pk, pv, cu, mx = self.cache.build_packed_kv(seq_ids, layer_idx)
+            o = attn_decode(q, pk, pv, None, cu, mx, N)
+            h = h + attn.o_proj(o.reshape(N, -1))
+            h = h + blk.mlp(blk.post_attention_layernorm(h))
+        h = self.norm(h)
+        return self.lm_head(h), h
+
+
+# ---------------------------------------------------------------------------
+# rollout (generator.py:54-497)
+# ---------------------------------------------------------------------------
+class TreeRollout:
+    """The entropy-gated tree rollout of ``MentatGenerator`` (same knobs and defaults)."""
+
+    def __init__(self, model, *, eos_token_id=2, max_active_branches: int = 10, branching_factor: int = 3,
+                 relative_entropy_multiplier: float = 1.25, entropy_ema_alpha: float = 0.3,
+                 max_new_tokens: int = 256, temperature: float = 0.7, repetition_penalty: float = 1.2,
+                 block_size: int = 16, max_blocks: int = 8192, semantic_similarity_threshold: float = 0.85,
+                 ema_alpha: float = 0.3, min_steps_before_prune: int = 5, soft_explore_window: int = 10,
+                 soft_explore_initial: float = 0.3, max_seqs: int = 256):
+        cfg = model.config
+        dev = next(model.parameters()).device
+        dtype = next(model.parameters()).dtype
+        hq = cfg.num_attention_heads
+        hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // hq
+        self.cache = PagedKVCacheManager(cfg.num_hidden_layers, cfg.num_key_value_heads, hd, max_blocks, block_size,
+                                         dev, dtype, max_seqs=max_seqs)
+        self.lm = PagedLM(model, self.cache)
+        self.eos = set(eos_token_id) if isinstance(eos_token_id, (list, tuple)) else {eos_token_id}
+        self.M, self.K = max_active_branches, branching_factor
+        self.max_new_tokens = max_new_tokens
+        self.sim_threshold, self.ema_alpha = semantic_similarity_threshold, ema_alpha
+        self.min_steps_before_prune = min_steps_before_prune
+        self.gate_cfg = GateConfig(temperature=temperature, repetition_penalty=repetition_penalty,
+                                   entropy_ema_alpha=entropy_ema_alpha,
+                                   relative_entropy_multiplier=relative_entropy_multiplier,
+                                   soft_explore_initial=soft_explore_initial, branching_factor=branching_factor,
+                                   max_active_branches=max_active_branches, soft_explore_window=soft_explore_window)
+        self.device = dev
+        self.decode_tokens = 0       # one per active leaf per decode step (step 0 excluded)
+        self.decode_time_s = 0.0
+        self.steps = 0
+
+    # ---- per-leaf decision (generator.py:250-374) ---------------------------
+    def _apply(self, tree: Tree, leaf: Node, rec, step: int) -> None:
+        leaf.entropy_ema = float(rec["ema"])
+        if int(rec["branch"]):
+            kids = tree.branch(leaf, rec["topk_ids"][: self.K].tolist(), rec["topk_lps"][: self.K].tolist())
+            for c in kids:
+                c.creation_step = step
+                self._eos(c)
+        else:
+            tree.extend(leaf, int(rec["argmax"]), float(rec["argmax_lp"]))
+            self._eos(leaf)
+
+    def _eos(self, node: Node) -> None:
+        if node.token_ids[-1] in self.eos:
+            node.is_eos, node.is_active = True, False
+            if node.seq_id is not None:
+                self.cache.free_sequence(node.seq_id)
+                node.seq_id = None
+
+    def _prune_similar(self, tree: Tree, step: int) -> None:                   # :400-497
+        cand = [lf for lf in tree.active_leaves()
+                if lf.semantic_vector is not None and step - lf.creation_step >= self.min_steps_before_prune]
+        m = len(cand)
+        if m <= 1:
+            return
+        v = F.normalize(torch.stack([lf.semantic_vector for lf in cand]), p=2, dim=1)
+        sim = v @ v.t()
+        mask = torch.triu(torch.ones(m, m, device=sim.device, dtype=torch.bool), diagonal=1)
+        for i in range(m):
+            for j in range(i + 1, m):
+                if cand[i].parent is not None and cand[i].parent is cand[j].parent:
+                    mask[i, j] = False
+        pairs = ((sim * mask) > self.sim_threshold).nonzero(as_tuple=False).tolist()
+        gone = set()
+        for i, j in pairs:
+            a, b = cand[i], cand[j]
+            if a.node_id in gone or b.node_id in gone:
+                continue
+            gone.add(b.node_id if a.cumulative_log_prob >= b.cumulative_log_prob else a.node_id)
+        for lf in cand:
+            if lf.node_id in gone and lf.is_active:
+                tree.prune(lf)
+
+    # ---- rollout -------------------------------------------------------------
+    def generate(self, prompt_ids) -> list:
+        return self.generate_many([prompt_ids])[0]
+
+    def generate_many(self, prompts) -> list:
+        """Rolls out one tree per prompt (token-id sequences), all in lockstep."""
+        trees, gates = [], []
+        for p in prompts:
+            ids = torch.as_tensor(p, dtype=torch.long, device=self.device)
+            sid = self.cache.allocate_sequence()
+            logits = self.lm.prefill(ids, sid)
+            tree = Tree(self.cache)
+            first = Node(node_id=tree.new_id(), seq_id=sid, parent=tree.root)
+            tree.root.children[0] = first
+            gate = Gate(self.device, self.gate_cfg)
+            gate.launch(logits.view(1, -1), [[]], [None], num_active=1, step=0)
+            self._apply(tree, first, gate.result()[0], 0)
+            trees.append(tree)
+            gates.append(gate)
+        torch.cuda.synchronize(self.device)
+        t0 = time.perf_counter()
+        for step in range(1, self.max_new_tokens):
+            per_tree = [t.active_leaves() for t in trees]
+            leaves = [lf for lv in per_tree for lf in lv]
+            if not leaves:
+                break
+            self.steps += 1
+            tokens = torch.tensor([lf.token_ids[-1] for lf in leaves], dtype=torch.long).to(self.device,
+                                                                                              non_blocking=True)
+            logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])
+            self.decode_tokens += len(leaves)
+            for i, lf in enumerate(leaves):                                    # :376-398
+                if lf.semantic_vector is None:
+                    lf.semantic_vector = hidden[i].clone()
+                else:
+                    lf.semantic_vector.mul_(1.0 - self.ema_alpha).add_(hidden[i], alpha=self.ema_alpha)
+            # one gate launch per tree (its own active count), then one wait
+            a = 0
+            for lv, gate in zip(per_tree, gates):
+                if lv:
+                    gate.launch(logits[a:a + len(lv)], [lf.full_sequence() for lf in lv],
+                                [lf.entropy_ema for lf in lv], num_active=len(lv), step=step)
+                a += len(lv)
+            for tree, lv, gate in zip(trees, per_tree, gates):
+                if not lv:
+                    continue
+                recs = gate.result()
+                for lf, rec in zip(lv, recs):
+                    if lf.is_active:
+                        self._apply(tree, lf, rec, step)
+                self._prune_similar(tree, step)
+        torch.cuda.synchronize(self.device)
+        self.decode_time_s += time.perf_counter() - t0
+        out = []
+        for tree in trees:
+            res = []
+            for node in tree.finished() + tree.active_leaves():
+                tids = node.full_sequence()
+                res.append({"token_ids": tids, "log_prob": node.cumulative_log_prob,
+                            "norm_prob": math.exp(node.cumulative_log_prob / max(len(tids), 1))})
+            tree.free_all()
+            res.sort(key=lambda r: r["norm_prob"], reverse=True)
+            out.append(res)
+        return out
+
+    def tree_tokens_per_s(self) -> float:
+        """Decode tokens per second of decode wall time (``generator.py:508-511``)."""
+        return self.decode_tokens / self.decode_time_s if self.decode_time_s > 0 else 0.0

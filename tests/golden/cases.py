@@ -170,3 +170,36 @@ def gate_inputs(c):
                    + np.float32(c["offset"]))
     hist = [int(h) for h in rng.integers(0, c["V"], c["hist"])]
     return x, hist
+
+
+# ---------------------------------------------------------------------------
+# entropy-gated rollouts (core/generator.py) on tiny seeded models, fp32 so that
+# the decode path's 1e-5 agreement keeps every branch / extend decision exact
+# ---------------------------------------------------------------------------
+ROLLOUT_CASES = {
+    "qwen3_fp32": dict(family="qwen3", seed=11, layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64,
+                       intermediate=512, vocab=512, prompts=3, prompt_len=24, max_new_tokens=28,
+                       max_active_branches=6, branching_factor=3, eos=2),
+    "llama_fp32": dict(family="llama", seed=12, layers=2, hidden=256, heads=4, kv_heads=1, head_dim=64,
+                       intermediate=512, vocab=384, prompts=2, prompt_len=17, max_new_tokens=24,
+                       max_active_branches=8, branching_factor=2, eos=3),
+}
+
+
+def rollout_model(c, device="cpu"):
+    """The case's randomly initialised model (same weights on any device)."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM, Qwen3Config, Qwen3ForCausalLM
+    kw = dict(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
+              num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
+              head_dim=c["head_dim"], max_position_embeddings=4096, eos_token_id=c["eos"])
+    torch.manual_seed(c["seed"])
+    model = (Qwen3ForCausalLM(Qwen3Config(**kw)) if c["family"] == "qwen3" else
+             LlamaForCausalLM(LlamaConfig(**kw)))
+    return model.to(device=device, dtype=torch.float32).eval()
+
+
+def rollout_prompts(c):
+    rng = np.random.default_rng(c["seed"] + 1000)
+    # ids >= 4 keep the prompt clear of the EOS id
+    return [rng.integers(4, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]

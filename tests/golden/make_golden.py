@@ -180,7 +180,44 @@ def make_gate():
     print("gate cases", len(res))
 
 
+class _StubTokenizer:
+    """The generator's tokenizer interface over space-separated token ids."""
+
+    def __init__(self, eos):
+        self.eos_token_id = eos
+
+    def __call__(self, prompt, return_tensors="pt"):
+        return {"input_ids": torch.tensor([[int(t) for t in prompt.split()]], dtype=torch.long)}
+
+    def decode(self, ids, skip_special_tokens=True):
+        return " ".join(str(int(t)) for t in ids)
+
+
+def make_rollout():
+    from tests.golden.cases import ROLLOUT_CASES, rollout_model, rollout_prompts
+    torch.set_num_threads(1)
+    out = {}
+    for name, c in ROLLOUT_CASES.items():
+        model = rollout_model(c)
+        runs = []
+        for prompt in rollout_prompts(c):
+            gen = MentatGenerator(model, _StubTokenizer(c["eos"]), max_active_branches=c["max_active_branches"],
+                                  branching_factor=c["branching_factor"], max_new_tokens=c["max_new_tokens"],
+                                  block_size=16, max_blocks=2048)
+            res = gen.generate(" ".join(map(str, prompt)))
+            d = gen.get_diagnostics()
+            runs.append({"results": [{"token_ids": r["token_ids"], "log_prob": r["log_prob"]} for r in res],
+                         "branch_points": [[s, n] for s, _, n in d["branch_points"]],
+                         "active_branch_trace": d["active_branch_trace"],
+                         "decode_tokens_total": d["decode_tokens_total"],
+                         "diversity_pruning_events": d["diversity_pruning_events"]})
+        out[name] = runs
+    with open(HERE / "rollout.json", "w") as f:
+        json.dump(out, f)
+
+
 if __name__ == "__main__":
     make_alloc_streams()
     make_attention()
     make_gate()
+    make_rollout()
