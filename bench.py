@@ -160,6 +160,80 @@ def build_tree(seed, device, extra_blocks):
     return m, kids, q, suf
 
 
+TREE_CONFIGS = {
+    # Qwen3-0.6B architecture, random init, bf16; 4 prompts of 256
+    # uniform-random ids, 256 new tokens, at most 8 leaves per tree, KV block 16
+    2: dict(family="qwen3", vocab=151936, hidden=1024, intermediate=3072, layers=28, heads=16, kv_heads=8,
+            head_dim=128, prompts=4, prompt_len=256, max_new_tokens=256, max_active=8, eos=151645),
+}
+
+
+def run_tree(args):
+    """Tree tokens/s of the entropy-gated rollout (``generator.py:508-511``): decode
+    tokens (one per active leaf per step) over decode wall time, summed over the
+    trees; every rank rolls out its own prompts (weak scaling)."""
+    import torch.distributed as dist
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from mentat_b200 import _lib
+    from mentat_b200.rollout import TreeRollout
+    rank, world, local = _env_rank()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    c = TREE_CONFIGS[args.tree_config]
+    cfg = Qwen3Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], max_position_embeddings=40960,
+                      rms_norm_eps=1e-6, tie_word_embeddings=True, eos_token_id=c["eos"])
+    torch.manual_seed(args.seed)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    rng = np.random.default_rng(args.seed * 1000 + rank)
+    prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
+    r = TreeRollout(model, eos_token_id=c["eos"], max_active_branches=c["max_active"],
+                    max_new_tokens=c["max_new_tokens"], max_blocks=16384)
+    lib = _lib.load()
+    r.generate_many(prompts)  # warm-up: captures the decode graphs
+    r.decode_tokens, r.decode_time_s, r.steps = 0, 0.0, 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.mentat_kernel_launch_count()
+    clocks = Clocks("GPU-" + str(torch.cuda.get_device_properties(device).uuid))
+    clocks.start()
+    results = r.generate_many(prompts)
+    clk = clocks.stop()
+    launches = lib.mentat_kernel_launch_count() - launches0
+    t = torch.tensor([r.decode_time_s], dtype=torch.float64, device=device)
+    tok = torch.tensor([float(r.decode_tokens)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tok, op=dist.ReduceOp.SUM)
+    secs, tokens = float(t.item()), float(tok.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"tree tokens/s (config {args.tree_config})", "value": round(tokens / secs, 2),
+            "unit": "tokens/s", "n_gpus": world, "steps": r.steps, "warmup": 1,
+            "ms_per_step": secs / max(r.steps, 1) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, seeded uniform-random prompt ids)",
+            "config": {"workload": f"BASELINE config {args.tree_config}: Qwen3-0.6B architecture, "
+                                   f"{c['prompts']} prompts x {c['prompt_len']} ids per rank, "
+                                   f"{c['max_new_tokens']} new tokens, <= {c['max_active']} leaves per tree",
+                       "decode_tokens": int(tokens), "trees_per_rank": c["prompts"],
+                       "leaves_per_tree_final": [len(x) for x in results],
+                       "parallelism": f"independent trees x{world}"},
+            "gpu_launches": int(launches),  # counted by the library; graph replays launch inside the graphs
+            "clocks": clk,
+            "note": "decode steps run as CUDA graphs; all trees of a rank advance in lockstep, one forward pass "
+                    "per step; the warm-up rollout captures the graphs",
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_profile_case(args):
     """A smaller tree for a profiler capture: warm-up calls, then --steps decode
     calls of attn_decode; prints the mean time per call (no JSON line)."""
@@ -400,10 +474,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-case", default=None, metavar="PREFIX,BRANCHES,SUFFIX",
                     help="time a smaller tree for a profiler capture instead of the benchmark")
+    ap.add_argument("--tree-config", type=int, default=None, choices=sorted(TREE_CONFIGS),
+                    help="tree tokens/s of the entropy-gated rollout on a BASELINE model config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile_case:
         run_profile_case(args)
+    elif args.tree_config is not None:
+        run_tree(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

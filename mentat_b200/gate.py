@@ -77,13 +77,14 @@ class Gate:
         n, V = logits.shape
         if logits.stride(1) != 1:
             logits = logits.contiguous()
-        nh = sum(len(h) for h in histories)
+        lens = [len(h) for h in histories]
+        nh = sum(lens)
         self._ensure(n, nh)
         ptr = np.zeros(n + 1, np.int32)
-        ptr[1:] = np.cumsum([len(h) for h in histories])
+        ptr[1:] = np.cumsum(lens)
         self._ptr_host.numpy()[: n + 1] = ptr
         if nh:
-            self._hist_host.numpy()[:nh] = np.fromiter((t for h in histories for t in h), np.int32, nh)
+            self._hist_host.numpy()[:nh] = np.concatenate([np.asarray(h, dtype=np.int32) for h in histories if len(h)])
         self._ema_host.numpy()[:n] = [math.nan if e is None else e for e in ema_old]
         self._ptr_dev[: n + 1].copy_(self._ptr_host[: n + 1], non_blocking=True)
         if nh:

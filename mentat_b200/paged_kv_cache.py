@@ -360,6 +360,22 @@ class PagedKVCacheManager:
         seq.num_blocks[layer], seq.tokens_in_last_block[layer] = nb, tf
         seq.num_tokens[layer] += n
 
+    def mirror_decode_step(self, seq_ids) -> None:
+        """Host bookkeeping of one token appended to every layer of each sequence,
+        for callers that append on the device without going through this class
+        (a replayed CUDA graph of the decode step)."""
+        for s in seq_ids:
+            seq = self._sequences[s]
+            if len(set(seq.num_tokens)) == 1 and len(set(seq.num_blocks)) == 1:
+                self._mirror_append(seq, 0, 1)
+                n0, b0, t0 = seq.num_tokens[0], seq.num_blocks[0], seq.tokens_in_last_block[0]
+                seq.num_tokens[:] = [n0] * self.num_layers
+                seq.num_blocks[:] = [b0] * self.num_layers
+                seq.tokens_in_last_block[:] = [t0] * self.num_layers
+            else:
+                for layer in range(self.num_layers):
+                    self._mirror_append(seq, layer, 1)
+
     def append_tokens(self, seq_id: int, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
         seq = self._sequences[seq_id]                       # :178-225
         n = k.shape[0]

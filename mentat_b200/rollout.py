@@ -57,15 +57,12 @@ class Node:
     entropy_ema: Optional[float] = None
     creation_step: int = 0
     is_pruned: bool = False
+    # generated token ids from the root to this node (the prompt is not part),
+    # kept up to date by Tree.extend / Tree.branch
+    seq: list = field(default_factory=list)
 
     def full_sequence(self) -> list:
-        """Generated token ids from the root to this node (the prompt is not part)."""
-        parts, node = [], self
-        while node is not None:
-            if node.token_ids:
-                parts.append(node.token_ids)
-            node = node.parent
-        return [t for seg in reversed(parts) for t in seg]
+        return self.seq
 
 
 class Tree:
@@ -82,6 +79,7 @@ class Tree:
 
     def extend(self, leaf: Node, token: int, log_prob: float) -> None:        # :89-99
         leaf.token_ids.append(token)
+        leaf.seq.append(token)
         leaf.cumulative_log_prob += log_prob
         leaf.depth += 1
 
@@ -91,7 +89,8 @@ class Tree:
             child = Node(node_id=self.new_id(), token_ids=[int(t)], seq_id=self.cache.fork_sequence(leaf.seq_id),
                          parent=leaf, cumulative_log_prob=leaf.cumulative_log_prob + float(lp), depth=leaf.depth + 1,
                          entropy_ema=leaf.entropy_ema,
-                         semantic_vector=None if leaf.semantic_vector is None else leaf.semantic_vector.clone())
+                         semantic_vector=None if leaf.semantic_vector is None else leaf.semantic_vector.clone(),
+                         seq=leaf.seq + [int(t)])
             leaf.children[child.node_id] = child
             kids.append(child)
         leaf.is_active = False
@@ -187,10 +186,63 @@ class PagedLM:
             h = h + blk.mlp(blk.post_attention_layernorm(h))
         return self.lm_head(self.norm(h)[0, -1])
 
+    # ---- CUDA-graph decode ----------------------------------------------------
+    # One graph per number of sequences N captures the whole multi-layer decode
+    # step: embedding, every layer (the append and decode operators included)
+    # and the lm_head.  The token ids and cache slots are static buffers filled
+    # before a replay; RoPE positions are read on the device from the cache's
+    # lengths, and the decode kernels plan from the device tables, so a replay
+    # needs no host work beyond the host mirror of the lengths.
+    _graphs = None
+
+    def enable_graphs(self, max_len: int, max_n: int) -> None:
+        """Decode through CUDA graphs; ``max_len`` bounds every sequence's length
+        and ``max_n`` the sequences of one step (they size the shared workspace,
+        which captured graphs must not see reallocated)."""
+        self.cache.decode_workspace(max_n, self.hq, max_len)
+        self._graph_max_len = max_len
+        self._graph_max_n = max_n
+        self._graphs = {}
+        self._pool = torch.cuda.graph_pool_handle()
+
+    def _forward_static(self, tokens: torch.Tensor, slots: torch.Tensor) -> tuple:
+        c = self.cache
+        N = tokens.shape[0]
+        h = self.embed(tokens)
+        pos = c._ntok[0].index_select(0, slots).to(torch.long).view(N, 1)  # lengths before this token
+        cos, sin = self.rotary(h, pos)
+        scale = 1.0 / (self.hd ** 0.5)
+        for layer_idx, blk in enumerate(self.layers):
+            attn = blk.self_attn
+            q, k, v = self._qkv(attn, blk.input_layernorm(h), (N,))
+            q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
+            torch.ops.mentat_b200.append_batched(c._k_all, c._v_all, slots, k, v, c._op_id, layer_idx)
+            o = torch.ops.mentat_b200.paged_decode(q, slots, self._graph_max_len, c._op_id, layer_idx, scale)
+            h = h + attn.o_proj(o.reshape(N, -1))
+            h = h + blk.mlp(blk.post_attention_layernorm(h))
+        h = self.norm(h)
+        return self.lm_head(h), h
+
+    def _capture(self, N: int) -> dict:
+        g = {"tokens": torch.zeros(N, dtype=torch.long, device=self.cache.device),
+             "slots": torch.zeros(N, dtype=torch.int32, device=self.cache.device),
+             "graph": torch.cuda.CUDAGraph()}
+        with torch.cuda.graph(g["graph"], pool=self._pool):
+            g["logits"], g["hidden"] = self._forward_static(g["tokens"], g["slots"])
+        self._graphs[N] = g
+        return g
+
     @torch.no_grad()
     def decode(self, tokens: torch.Tensor, seq_ids: list) -> tuple:
         """One token per sequence: logits (N, V) and final hidden states (N, D)."""
         N = len(seq_ids)
+        if self._graphs is not None and N <= self._graph_max_n:
+            g = self._graphs.get(N) or self._capture(N)
+            g["tokens"].copy_(tokens.view(N))
+            g["slots"].copy_(self.cache._slots_dev(seq_ids))
+            g["graph"].replay()
+            self.cache.mirror_decode_step(seq_ids)
+            return g["logits"], g["hidden"]
         h = self.embed(tokens.view(N))
         pos = torch.tensor([self.cache.get_kv_length(s) for s in seq_ids], device=h.device).view(N, 1)
         cos, sin = self.rotary(h, pos)  # (N, 1, hd): broadcasts over heads
@@ -219,7 +271,8 @@ class TreeRollout:
                  max_new_tokens: int = 256, temperature: float = 0.7, repetition_penalty: float = 1.2,
                  block_size: int = 16, max_blocks: int = 8192, semantic_similarity_threshold: float = 0.85,
                  ema_alpha: float = 0.3, min_steps_before_prune: int = 5, soft_explore_window: int = 10,
-                 soft_explore_initial: float = 0.3, max_seqs: int = 256):
+                 soft_explore_initial: float = 0.3, max_seqs: int = 256, cuda_graphs: bool = True,
+                 max_prompt_len: int = 4096):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -239,6 +292,8 @@ class TreeRollout:
                                    soft_explore_initial=soft_explore_initial, branching_factor=branching_factor,
                                    max_active_branches=max_active_branches, soft_explore_window=soft_explore_window)
         self.device = dev
+        self.cuda_graphs = cuda_graphs
+        self.max_prompt_len = max_prompt_len
         self.decode_tokens = 0       # one per active leaf per decode step (step 0 excluded)
         self.decode_time_s = 0.0
         self.steps = 0
@@ -271,10 +326,10 @@ class TreeRollout:
         v = F.normalize(torch.stack([lf.semantic_vector for lf in cand]), p=2, dim=1)
         sim = v @ v.t()
         mask = torch.triu(torch.ones(m, m, device=sim.device, dtype=torch.bool), diagonal=1)
-        for i in range(m):
-            for j in range(i + 1, m):
-                if cand[i].parent is not None and cand[i].parent is cand[j].parent:
-                    mask[i, j] = False
+        # siblings (same parent) are not compared: their vectors started equal
+        par = torch.tensor([id(lf.parent) if lf.parent is not None else -1 - i for i, lf in enumerate(cand)],
+                           dtype=torch.int64).to(sim.device, non_blocking=True)
+        mask &= par.view(m, 1) != par.view(1, m)
         pairs = ((sim * mask) > self.sim_threshold).nonzero(as_tuple=False).tolist()
         gone = set()
         for i, j in pairs:
@@ -305,6 +360,12 @@ class TreeRollout:
             self._apply(tree, first, gate.result()[0], 0)
             trees.append(tree)
             gates.append(gate)
+        if self.cuda_graphs and self.lm._graphs is None:
+            longest = max(len(p) for p in prompts)
+            # a step decodes at most every tree's live leaves, which stay within
+            # max_active_branches + the K - 1 extra children of a last branch each
+            self.lm.enable_graphs(max(longest, self.max_prompt_len) + self.max_new_tokens + 1,
+                                  min(self.cache.max_seqs, len(prompts) * (self.M + self.K * self.M)))
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         for step in range(1, self.max_new_tokens):
