@@ -234,6 +234,69 @@ def run_tree(args):
         dist.destroy_process_group()
 
 
+def run_profile_kernels(args):
+    """The gate and the append kernels on benchmark-sized inputs, for a profiler
+    capture: the gate over 32 leaves x 151936 bf16 logits (config 2's vocabulary)
+    with 200-token histories, and one-token batched appends to the 64 branches of
+    the config-4 tree (the first append after the forks copies every branch's
+    partial tail block).  Prints time per call and algorithmic GB/s."""
+    from mentat_b200.gate import GATE_OUT_DTYPE, Gate, GateConfig
+    device = torch.device("cuda", 0)
+    steps = max(args.steps, 1)
+    n, V = 32, 151936
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    logits = (torch.randn((n, V), generator=g, device=device) * 2.0).to(torch.bfloat16)
+    rng = np.random.default_rng(args.seed)
+    hist = [rng.integers(0, V, 200).tolist() for _ in range(n)]
+    gate = Gate(device, GateConfig(max_active_branches=64))
+    for _ in range(args.warmup):
+        gate.launch(logits, hist, [5.0] * n, num_active=n, step=3)
+        gate.result()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        gate.launch(logits, hist, [5.0] * n, num_active=n, step=3)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # the kernel alone: the same operator call, `steps` times in one CUDA graph
+    c = gate.cfg
+    nb = n * GATE_OUT_DTYPE.itemsize
+    op_args = (logits, gate._ptr_dev[: n + 1], gate._hist_dev, gate._ema_dev[:n],
+               [c.temperature, c.repetition_penalty, c.entropy_ema_alpha, c.relative_entropy_multiplier,
+                c.soft_explore_initial],
+               [c.branching_factor, c.max_active_branches, n, 3, c.soft_explore_window], gate._out_dev[:nb])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(steps):
+            torch.ops.mentat_b200.gate_step(*op_args)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    kms = e0.elapsed_time(e1) / steps
+    del graph
+    print(f"gate: {n} x {V} bf16 logits, {ms * 1e3:.1f} us/call through Gate.launch, {kms * 1e3:.1f} us/kernel "
+          f"({n * V * 2 / kms / 1e6:.1f} GB/s of logits)", flush=True)
+    m, kids, q, suf = build_tree(args.seed, device, extra_blocks=NBR * (args.warmup + steps + 2))
+    kv = torch.randn((args.warmup + steps, 2, NBR, HKV, D), generator=g, device=device).to(torch.bfloat16)
+    for i in range(args.warmup):
+        m.append_tokens_batched(kids, 0, kv[i, 0], kv[i, 1])
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(steps):
+        m.append_tokens_batched(kids, 0, kv[args.warmup + i, 0], kv[args.warmup + i, 1])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    nb = NBR * HKV * D * 2 * ELEM
+    print(f"append: {NBR} sequences x 1 token, {ms * 1e3:.1f} us/call, {nb / ms / 1e6:.2f} GB/s of K/V rows",
+          flush=True)
+    m.check()
+
+
 def run_profile_case(args):
     """A smaller tree for a profiler capture: warm-up calls, then --steps decode
     calls of attn_decode; prints the mean time per call (no JSON line)."""
@@ -474,12 +537,16 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-case", default=None, metavar="PREFIX,BRANCHES,SUFFIX",
                     help="time a smaller tree for a profiler capture instead of the benchmark")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="time the gate and append kernels for a profiler capture instead of the benchmark")
     ap.add_argument("--tree-config", type=int, default=None, choices=sorted(TREE_CONFIGS),
                     help="tree tokens/s of the entropy-gated rollout on a BASELINE model config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile_case:
         run_profile_case(args)
+    elif args.profile_kernels:
+        run_profile_kernels(args)
     elif args.tree_config is not None:
         run_tree(args)
     elif args.impl == "reference":
