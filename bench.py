@@ -199,12 +199,12 @@ def run_tree(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    launches0 = lib.mentat_kernel_launch_count()
+    launches0 = lib.mentat_kernel_launch_count() + r.lm.graph_kernel_launches
     clocks = Clocks("GPU-" + str(torch.cuda.get_device_properties(device).uuid))
     clocks.start()
     results = r.generate_many(prompts)
     clk = clocks.stop()
-    launches = lib.mentat_kernel_launch_count() - launches0
+    launches = lib.mentat_kernel_launch_count() + r.lm.graph_kernel_launches - launches0
     t = torch.tensor([r.decode_time_s], dtype=torch.float64, device=device)
     tok = torch.tensor([float(r.decode_tokens)], dtype=torch.float64, device=device)
     if world > 1:
@@ -224,7 +224,7 @@ def run_tree(args):
                        "decode_tokens": int(tokens), "trees_per_rank": c["prompts"],
                        "leaves_per_tree_final": [len(x) for x in results],
                        "parallelism": f"independent trees x{world}"},
-            "gpu_launches": int(launches),  # counted by the library; graph replays launch inside the graphs
+            "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
             "clocks": clk,
             "note": "decode steps run as CUDA graphs; all trees of a rank advance in lockstep, one forward pass "
                     "per step; the warm-up rollout captures the graphs",

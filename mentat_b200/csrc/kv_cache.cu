@@ -334,59 +334,70 @@ __global__ void k_append_data(mentat_kv_cache c, int layer, int n, const uint8_t
 // into the CoW'd block.  Only the first chunk can copy: later chunks get fresh
 // (unshared) blocks.
 // ---------------------------------------------------------------------------
-__global__ void k_append_multi_plan(mentat_kv_cache c, int layer, int slot, int n) {
+// The reference's loop (:196-222) allocates in this order: a copy of a shared,
+// partially filled tail block on the first chunk (the only chunk whose tail can
+// be shared: later blocks are fresh), then one fresh block per further
+// bs tokens.  Those are consecutive pops of the free FIFO, so thread 0 settles
+// the copy and the counts and the CTA fills the fresh table entries at once.
+constexpr int MULTI_PLAN_THREADS = 256;
+__global__ void __launch_bounds__(MULTI_PLAN_THREADS) k_append_multi_plan(mentat_kv_cache c, int layer, int slot,
+                                                                          int n) {
+    __shared__ int s_nb, s_fresh, s_pop0, s_stop;
+    __shared__ long long s_head;
     int32_t* sc = c.scratch;
-    if (has_error(c)) {
-        sc[0] = 2;
-        return;
-    }
     const int64_t si = seq_index(c, layer, slot);
     int32_t* row = table_row(c, layer, slot);
-    int nb = c.nblocks[si], tf = c.tail[si];
-    sc[0] = 0;
-    sc[1] = -1;
-    sc[2] = -1;
-    sc[3] = c.ntok[si];
-    sc[4] = 0;
-    int written = 0;
-    bool first = true;
-    while (written < n) {
-        if (nb == 0 || tf == c.block_size) {
-            if (nb >= c.max_blocks_per_seq) {
-                set_error(c, MENTAT_DEV_TABLE_OVERFLOW, slot);
-                sc[0] = 2;
-                return;
+    const int bs = c.block_size;
+    if (threadIdx.x == 0) {
+        s_stop = 1;
+        sc[0] = 0;
+        sc[1] = -1;
+        sc[2] = -1;
+        sc[3] = c.ntok[si];
+        sc[4] = 0;
+        const int nb = c.nblocks[si], tf = c.tail[si];
+        const int room = (nb > 0 && tf < bs) ? bs - tf : 0;  // rows left in the current tail block
+        const int t = nb > 0 ? row[nb - 1] : -1;
+        const int cow = (n > 0 && room > 0 && c.refcounts[t] > 1) ? 1 : 0;
+        const int rest = n - min(n, room);
+        const int fresh = (rest + bs - 1) / bs;
+        const long long head = c.ctrl[MENTAT_CTRL_HEAD], tail = c.ctrl[MENTAT_CTRL_TAIL];
+        if (has_error(c)) {
+            sc[0] = 2;
+        } else if (nb + fresh > c.max_blocks_per_seq) {
+            set_error(c, MENTAT_DEV_TABLE_OVERFLOW, slot);
+            sc[0] = 2;
+        } else if (tail - head < cow + fresh) {
+            set_error(c, MENTAT_DEV_OUT_OF_BLOCKS, c.num_blocks);
+            sc[0] = 2;
+        } else if (n > 0) {
+            if (cow) {
+                const int b = ring_at(c, head, 0);
+                c.refcounts[b] = 1;
+                release_one(c, t);  // still referenced elsewhere: never freed here
+                row[nb - 1] = b;
+                sc[1] = t;
+                sc[2] = b;
+                sc[4] = min(room, n);
             }
-            int b = alloc_one(c);
-            if (b < 0) {
-                sc[0] = 2;
-                return;
-            }
-            row[nb++] = b;
-            tf = 0;
+            note_allocs(c, cow + fresh, cow);
+            c.nblocks[si] = nb + fresh;
+            c.tail[si] = fresh ? rest - (fresh - 1) * bs : tf + n;
+            c.ntok[si] += n;
+            s_nb = nb;
+            s_fresh = fresh;
+            s_pop0 = cow;
+            s_head = head;
+            s_stop = 0;
         }
-        int t = row[nb - 1];
-        if (c.refcounts[t] > 1) {
-            int b = alloc_one(c);
-            if (b < 0) {
-                sc[0] = 2;
-                return;
-            }
-            release_one(c, t);
-            row[nb - 1] = b;
-            sc[1] = t;
-            sc[2] = b;
-            c.ctrl[MENTAT_CTRL_COWS] += 1;
-        }
-        int w = min(c.block_size - tf, n - written);
-        if (first) sc[4] = (sc[1] >= 0) ? w : 0;
-        first = false;
-        written += w;
-        tf += w;
     }
-    c.nblocks[si] = nb;
-    c.tail[si] = tf;
-    c.ntok[si] += n;
+    __syncthreads();
+    if (s_stop) return;
+    for (int j = threadIdx.x; j < s_fresh; j += blockDim.x) {
+        const int b = ring_at(c, s_head, s_pop0 + j);
+        c.refcounts[b] = 1;
+        row[s_nb + j] = b;
+    }
 }
 
 // CTA 0 owns the CoW'd block (copy first, then its tokens) so the copy cannot
@@ -605,7 +616,7 @@ int mentat_kv_append(const mentat_kv_cache* c, int32_t layer, int32_t slot, int3
         return MENTAT_ERR_ARG;
     if (n == 0) return MENTAT_OK;
     const int esz = dtype_bytes(c->dtype);
-    k_append_multi_plan<<<1, 1, 0, s>>>(*c, layer, slot, n);
+    k_append_multi_plan<<<1, MULTI_PLAN_THREADS, 0, s>>>(*c, layer, slot, n);
     MENTAT_CHECK_LAUNCH();
     int grid = n < 592 ? n + 1 : 593;
     k_append_multi_data<<<grid, 128, 0, s>>>(*c, layer, slot, n, (const uint8_t*)k, k_stride * esz,

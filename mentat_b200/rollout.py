@@ -31,9 +31,11 @@ import time
 from dataclasses import dataclass, field
 from typing import Optional
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from .attention_backend import attn_decode, attn_prefill
 from .gate import Gate, GateConfig
 from .paged_kv_cache import PagedKVCacheManager
@@ -42,6 +44,30 @@ from .paged_kv_cache import PagedKVCacheManager
 # ---------------------------------------------------------------------------
 # tree (generator_utils.py:40-189)
 # ---------------------------------------------------------------------------
+class _Hist:
+    """A leaf's generated token ids as a growable int32 array (the gate's
+    repetition-penalty history, handed to it without a list conversion)."""
+    __slots__ = ("buf", "n")
+
+    def __init__(self, buf=None, n: int = 0):
+        self.buf = np.empty(64, np.int32) if buf is None else buf
+        self.n = n
+
+    def append(self, t: int) -> None:
+        if self.n == self.buf.shape[0]:
+            self.buf = np.concatenate([self.buf, np.empty_like(self.buf)])
+        self.buf[self.n] = t
+        self.n += 1
+
+    def plus(self, t: int) -> "_Hist":
+        h = _Hist(self.buf.copy(), self.n)
+        h.append(t)
+        return h
+
+    def view(self) -> np.ndarray:
+        return self.buf[: self.n]
+
+
 @dataclass(eq=False)
 class Node:
     node_id: int
@@ -53,13 +79,14 @@ class Node:
     depth: int = 0
     is_active: bool = True
     is_eos: bool = False
-    semantic_vector: Optional[torch.Tensor] = None
+    sem_row: Optional[int] = None  # row of the rollout's semantic-vector table, once it has one
     entropy_ema: Optional[float] = None
     creation_step: int = 0
     is_pruned: bool = False
     # generated token ids from the root to this node (the prompt is not part),
-    # kept up to date by Tree.extend / Tree.branch
+    # kept up to date by Tree.extend / Tree.branch, as a list and as an array
     seq: list = field(default_factory=list)
+    hist: _Hist = field(default_factory=_Hist)
 
     def full_sequence(self) -> list:
         return self.seq
@@ -68,9 +95,10 @@ class Node:
 class Tree:
     """Branches of one rollout, each live leaf backed by a cache sequence."""
 
-    def __init__(self, cache: PagedKVCacheManager):
+    def __init__(self, cache: PagedKVCacheManager, sem=None):
         self.root = Node(node_id=0)
         self.cache = cache
+        self.sem = sem  # the rollout's semantic-vector table (children copy their parent's row)
         self._next = 1
 
     def new_id(self) -> int:
@@ -80,6 +108,7 @@ class Tree:
     def extend(self, leaf: Node, token: int, log_prob: float) -> None:        # :89-99
         leaf.token_ids.append(token)
         leaf.seq.append(token)
+        leaf.hist.append(token)
         leaf.cumulative_log_prob += log_prob
         leaf.depth += 1
 
@@ -88,9 +117,9 @@ class Tree:
         for t, lp in zip(tokens, log_probs):
             child = Node(node_id=self.new_id(), token_ids=[int(t)], seq_id=self.cache.fork_sequence(leaf.seq_id),
                          parent=leaf, cumulative_log_prob=leaf.cumulative_log_prob + float(lp), depth=leaf.depth + 1,
-                         entropy_ema=leaf.entropy_ema,
-                         semantic_vector=None if leaf.semantic_vector is None else leaf.semantic_vector.clone(),
-                         seq=leaf.seq + [int(t)])
+                         entropy_ema=leaf.entropy_ema, seq=leaf.seq + [int(t)], hist=leaf.hist.plus(int(t)))
+            if leaf.sem_row is not None and self.sem is not None:
+                child.sem_row = self.sem.copy_row(leaf.sem_row)
             leaf.children[child.node_id] = child
             kids.append(child)
         leaf.is_active = False
@@ -223,12 +252,19 @@ class PagedLM:
         h = self.norm(h)
         return self.lm_head(h), h
 
+    # kernels of this library run by graph replays (a replay launches no kernel
+    # from the host, so the library's own launch counter does not see them)
+    graph_kernel_launches = 0
+
     def _capture(self, N: int) -> dict:
         g = {"tokens": torch.zeros(N, dtype=torch.long, device=self.cache.device),
              "slots": torch.zeros(N, dtype=torch.int32, device=self.cache.device),
              "graph": torch.cuda.CUDAGraph()}
+        lib = _lib.load()
+        n0 = lib.mentat_kernel_launch_count()
         with torch.cuda.graph(g["graph"], pool=self._pool):
             g["logits"], g["hidden"] = self._forward_static(g["tokens"], g["slots"])
+        g["kernels"] = lib.mentat_kernel_launch_count() - n0
         self._graphs[N] = g
         return g
 
@@ -241,6 +277,7 @@ class PagedLM:
             g["tokens"].copy_(tokens.view(N))
             g["slots"].copy_(self.cache._slots_dev(seq_ids))
             g["graph"].replay()
+            self.graph_kernel_launches += g["kernels"]
             self.cache.mirror_decode_step(seq_ids)
             return g["logits"], g["hidden"]
         h = self.embed(tokens.view(N))
@@ -258,6 +295,68 @@ class PagedLM:
             h = h + blk.mlp(blk.post_attention_layernorm(h))
         h = self.norm(h)
         return self.lm_head(h), h
+
+
+# ---------------------------------------------------------------------------
+# semantic vectors (generator.py:376-398, 400-497)
+# ---------------------------------------------------------------------------
+class _SemTable:
+    """Every node's semantic vector, one row each of a device table: the EMA of
+    the leaf's final hidden states over its decode steps.  A branch's children
+    start from copies of the parent's row; the copies of a step are batched and
+    run before the next read of the table."""
+
+    def __init__(self, dim: int, dtype, device, cap: int = 256):
+        self.t = torch.empty((cap, dim), dtype=dtype, device=device)
+        self.n = 0
+        self._copies = []
+
+    def _alloc(self) -> int:
+        if self.n == self.t.shape[0]:
+            t = torch.empty((2 * self.n, self.t.shape[1]), dtype=self.t.dtype, device=self.t.device)
+            t[: self.n].copy_(self.t)
+            self.t = t
+        r, self.n = self.n, self.n + 1
+        return r
+
+    def _idx(self, rows) -> torch.Tensor:
+        return torch.tensor(rows, dtype=torch.long).to(self.t.device, non_blocking=True)
+
+    def copy_row(self, src: int) -> int:
+        dst = self._alloc()
+        self._copies.append((src, dst))
+        return dst
+
+    def flush(self) -> None:
+        if self._copies:
+            src, dst = zip(*self._copies)
+            self.t.index_copy_(0, self._idx(dst), self.t.index_select(0, self._idx(src)))
+            self._copies = []
+
+    def update(self, leaves, hidden: torch.Tensor, alpha: float) -> None:
+        """First step of a leaf: its hidden state; later: (1 - a) v + a h, with the
+        reference's two rounded steps (``v.mul_(1 - a).add_(h, alpha=a)``)."""
+        self.flush()
+        new_i, new_r, upd_i, upd_r = [], [], [], []
+        for i, lf in enumerate(leaves):
+            if lf.sem_row is None:
+                lf.sem_row = self._alloc()
+                new_i.append(i)
+                new_r.append(lf.sem_row)
+            else:
+                upd_i.append(i)
+                upd_r.append(lf.sem_row)
+        if new_i:
+            self.t.index_copy_(0, self._idx(new_r), hidden.index_select(0, self._idx(new_i)))
+        if upd_i:
+            rows = self._idx(upd_r)
+            v = self.t.index_select(0, rows)
+            v.mul_(1.0 - alpha).add_(hidden.index_select(0, self._idx(upd_i)), alpha=alpha)
+            self.t.index_copy_(0, rows, v)
+
+    def rows(self, rows) -> torch.Tensor:
+        self.flush()
+        return self.t.index_select(0, self._idx(rows))
 
 
 # ---------------------------------------------------------------------------
@@ -317,29 +416,46 @@ class TreeRollout:
                 self.cache.free_sequence(node.seq_id)
                 node.seq_id = None
 
-    def _prune_similar(self, tree: Tree, step: int) -> None:                   # :400-497
-        cand = [lf for lf in tree.active_leaves()
-                if lf.semantic_vector is not None and step - lf.creation_step >= self.min_steps_before_prune]
-        m = len(cand)
-        if m <= 1:
+    def _prune_similar(self, trees, step: int) -> None:                       # :400-497
+        """Semantic pruning of every tree of the step with one similarity matrix
+        and one host read: pairs are compared only inside a tree, never between
+        siblings, and each tree resolves its pairs in (i, j) order."""
+        groups = []
+        for tree in trees:
+            cand = [lf for lf in tree.active_leaves()
+                    if lf.sem_row is not None and step - lf.creation_step >= self.min_steps_before_prune]
+            if len(cand) > 1:
+                groups.append((tree, cand))
+        if not groups:
             return
-        v = F.normalize(torch.stack([lf.semantic_vector for lf in cand]), p=2, dim=1)
+        flat = [lf for _, cand in groups for lf in cand]
+        m = len(flat)
+        v = F.normalize(self.sem.rows([lf.sem_row for lf in flat]), p=2, dim=1)
         sim = v @ v.t()
-        mask = torch.triu(torch.ones(m, m, device=sim.device, dtype=torch.bool), diagonal=1)
-        # siblings (same parent) are not compared: their vectors started equal
-        par = torch.tensor([id(lf.parent) if lf.parent is not None else -1 - i for i, lf in enumerate(cand)],
+        key = torch.tensor([[g, id(lf.parent) if lf.parent is not None else -1 - i]
+                            for g, (_, cand) in enumerate(groups) for i, lf in enumerate(cand)],
                            dtype=torch.int64).to(sim.device, non_blocking=True)
-        mask &= par.view(m, 1) != par.view(1, m)
+        mask = torch.triu(torch.ones(m, m, device=sim.device, dtype=torch.bool), diagonal=1)
+        mask &= key[:, :1] == key[:, :1].t()   # same tree
+        mask &= key[:, 1:] != key[:, 1:].t()   # siblings (same parent) are not compared
         pairs = ((sim * mask) > self.sim_threshold).nonzero(as_tuple=False).tolist()
-        gone = set()
+        base, gone = [], []
+        off = 0
+        for _, cand in groups:
+            base.append(off)
+            gone.append(set())
+            off += len(cand)
+        owner = [g for g, (_, cand) in enumerate(groups) for _ in cand]
         for i, j in pairs:
-            a, b = cand[i], cand[j]
-            if a.node_id in gone or b.node_id in gone:
+            g = owner[i]
+            a, b = flat[i], flat[j]
+            if a.node_id in gone[g] or b.node_id in gone[g]:
                 continue
-            gone.add(b.node_id if a.cumulative_log_prob >= b.cumulative_log_prob else a.node_id)
-        for lf in cand:
-            if lf.node_id in gone and lf.is_active:
-                tree.prune(lf)
+            gone[g].add(b.node_id if a.cumulative_log_prob >= b.cumulative_log_prob else a.node_id)
+        for g, (tree, cand) in enumerate(groups):
+            for lf in cand:
+                if lf.node_id in gone[g] and lf.is_active:
+                    tree.prune(lf)
 
     # ---- rollout -------------------------------------------------------------
     def generate(self, prompt_ids) -> list:
@@ -348,11 +464,12 @@ class TreeRollout:
     def generate_many(self, prompts) -> list:
         """Rolls out one tree per prompt (token-id sequences), all in lockstep."""
         trees, gates = [], []
+        self.sem = _SemTable(self.lm.model.config.hidden_size, next(self.lm.model.parameters()).dtype, self.device)
         for p in prompts:
             ids = torch.as_tensor(p, dtype=torch.long, device=self.device)
             sid = self.cache.allocate_sequence()
             logits = self.lm.prefill(ids, sid)
-            tree = Tree(self.cache)
+            tree = Tree(self.cache, self.sem)
             first = Node(node_id=tree.new_id(), seq_id=sid, parent=tree.root)
             tree.root.children[0] = first
             gate = Gate(self.device, self.gate_cfg)
@@ -378,16 +495,12 @@ class TreeRollout:
                                                                                               non_blocking=True)
             logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])
             self.decode_tokens += len(leaves)
-            for i, lf in enumerate(leaves):                                    # :376-398
-                if lf.semantic_vector is None:
-                    lf.semantic_vector = hidden[i].clone()
-                else:
-                    lf.semantic_vector.mul_(1.0 - self.ema_alpha).add_(hidden[i], alpha=self.ema_alpha)
+            self.sem.update(leaves, hidden, self.ema_alpha)                    # :376-398
             # one gate launch per tree (its own active count), then one wait
             a = 0
             for lv, gate in zip(per_tree, gates):
                 if lv:
-                    gate.launch(logits[a:a + len(lv)], [lf.full_sequence() for lf in lv],
+                    gate.launch(logits[a:a + len(lv)], [lf.hist.view() for lf in lv],
                                 [lf.entropy_ema for lf in lv], num_active=len(lv), step=step)
                 a += len(lv)
             for tree, lv, gate in zip(trees, per_tree, gates):
@@ -397,7 +510,7 @@ class TreeRollout:
                 for lf, rec in zip(lv, recs):
                     if lf.is_active:
                         self._apply(tree, lf, rec, step)
-                self._prune_similar(tree, step)
+            self._prune_similar(trees, step)
         torch.cuda.synchronize(self.device)
         self.decode_time_s += time.perf_counter() - t0
         out = []
