@@ -162,39 +162,90 @@ def build_tree(seed, device, extra_blocks):
 
 TREE_CONFIGS = {
     # Qwen3-0.6B architecture, random init, bf16; 4 prompts of 256
-    # uniform-random ids, 256 new tokens, at most 8 leaves per tree, KV block 16
+    # uniform-random ids, 256 new tokens, at most 8 leaves per tree, KV block 16; one
+    # B200 (under torchrun every rank rolls out its own 4 prompts: weak scaling)
     2: dict(family="qwen3", vocab=151936, hidden=1024, intermediate=3072, layers=28, heads=16, kv_heads=8,
-            head_dim=128, prompts=4, prompt_len=256, max_new_tokens=256, max_active=8, eos=151645),
+            head_dim=128, rope_theta=1000000.0, prompts=4, prompt_len=256, max_new_tokens=256, max_active=8,
+            eos=151645, shard=False, graphs=True),
+    # Llama-3.1-8B architecture, random init, bf16; 64 prompts of
+    # 2048 ids, trees of up to 16 leaves, 512 new tokens; the 64 trees are sharded
+    # across the ranks (strong scaling)
+    3: dict(family="llama", vocab=128256, hidden=4096, intermediate=14336, layers=32, heads=32, kv_heads=8,
+            head_dim=128, rope_theta=500000.0, prompts=64, prompt_len=2048, max_new_tokens=512, max_active=16,
+            eos=128001, shard=True, graphs=False),
 }
+
+
+def tree_model(c, device, seed):
+    """A random-init model of a tree configuration's architecture, in bf16."""
+    torch.manual_seed(seed)
+    if c["family"] == "qwen3":
+        from transformers import Qwen3Config as Cfg, Qwen3ForCausalLM as Model
+        cfg = Cfg(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
+                  num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
+                  head_dim=c["head_dim"], max_position_embeddings=40960, rms_norm_eps=1e-6,
+                  rope_theta=c["rope_theta"], tie_word_embeddings=True, eos_token_id=c["eos"])
+    else:
+        from transformers import LlamaConfig as Cfg, LlamaForCausalLM as Model
+        cfg = Cfg(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
+                  num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
+                  head_dim=c["head_dim"], max_position_embeddings=131072, rms_norm_eps=1e-5,
+                  rope_theta=c["rope_theta"], tie_word_embeddings=False, eos_token_id=c["eos"],
+                  rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+    dt = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)  # initialise the weights in bf16 directly
+    try:
+        with torch.device(device):
+            model = Model(cfg).eval()
+    finally:
+        torch.set_default_dtype(dt)
+    return model
 
 
 def run_tree(args):
     """Tree tokens/s of the entropy-gated rollout (``generator.py:508-511``): decode
     tokens (one per active leaf per step) over decode wall time, summed over the
-    trees; every rank rolls out its own prompts (weak scaling)."""
+    trees.  The branch threshold is the 90th percentile of the gate entropies of a
+    seeded 32-step warm-up rollout (random-init weights make the adaptive
+    threshold meaningless).  Config 2: every rank rolls out its own prompts (weak
+    scaling); config 3: the prompts are split across the ranks (strong scaling)."""
     import torch.distributed as dist
-    from transformers import Qwen3Config, Qwen3ForCausalLM
     from mentat_b200 import _lib
     from mentat_b200.rollout import TreeRollout
     rank, world, local = _env_rank()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
     c = TREE_CONFIGS[args.tree_config]
-    cfg = Qwen3Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
-                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
-                      num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], max_position_embeddings=40960,
-                      rms_norm_eps=1e-6, tie_word_embeddings=True, eos_token_id=c["eos"])
-    torch.manual_seed(args.seed)
-    with torch.device(device):
-        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
-    rng = np.random.default_rng(args.seed * 1000 + rank)
-    prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
-    r = TreeRollout(model, eos_token_id=c["eos"], max_active_branches=c["max_active"],
-                    max_new_tokens=c["max_new_tokens"], max_blocks=16384)
+    model = tree_model(c, device, args.seed)
+    if c["shard"]:
+        rng = np.random.default_rng(args.seed * 1000)
+        allp = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
+        prompts = allp[rank::world]
+    else:
+        rng = np.random.default_rng(args.seed * 1000 + rank)
+        prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
+    M, K = c["max_active"], 3
+    n_trees = len(prompts)
+    # every live leaf of every tree at once, plus the children of one step's branches
+    max_seqs = n_trees * (M + K) + 16
+    # a tree's prompt blocks are shared; each live leaf owns at most its generated blocks + a CoW'd tail
+    blocks = n_trees * (-(-c["prompt_len"] // 16) + (M + K) * (-(-c["max_new_tokens"] // 16) + 2)) + 64
+    r = TreeRollout(model, eos_token_id=c["eos"], max_active_branches=M, branching_factor=K,
+                    max_new_tokens=c["max_new_tokens"], max_blocks=blocks, max_seqs=max_seqs,
+                    cuda_graphs=c["graphs"], static_decode=not c["graphs"], max_prompt_len=c["prompt_len"],
+                    max_blocks_per_seq=-(-(c["prompt_len"] + c["max_new_tokens"]) // 16) + 2)
     lib = _lib.load()
-    r.generate_many(prompts)  # warm-up: captures the decode graphs
+    thr = r.calibrate_threshold(prompts, steps=32, q=90.0)
+    if c["graphs"]:
+        r.generate_many(prompts)  # warm-up: captures the decode graphs
+    else:
+        full = r.max_new_tokens
+        r.max_new_tokens = 16     # warm-up of the eager path
+        r.generate_many(prompts)
+        r.max_new_tokens = full
     r.decode_tokens, r.decode_time_s, r.steps = 0, 0.0, 0
     if world > 1:
         dist.barrier()
@@ -211,23 +262,29 @@ def run_tree(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.all_reduce(tok, op=dist.ReduceOp.SUM)
     secs, tokens = float(t.item()), float(tok.item())
+    leaves = [len(x) for x in results]
     if rank == 0:
+        arch = {"qwen3": "Qwen3-0.6B", "llama": "Llama-3.1-8B"}[c["family"]]
         print(json.dumps({
             "metric": f"tree tokens/s (config {args.tree_config})", "value": round(tokens / secs, 2),
             "unit": "tokens/s", "n_gpus": world, "steps": r.steps, "warmup": 1,
-            "ms_per_step": secs / max(r.steps, 1) * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "ms_per_step": secs / max(r.steps, 1) * 1e3, "higher_is_better": True,
+            "scaling": "strong" if c["shard"] else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, seeded uniform-random prompt ids)",
-            "config": {"workload": f"BASELINE config {args.tree_config}: Qwen3-0.6B architecture, "
-                                   f"{c['prompts']} prompts x {c['prompt_len']} ids per rank, "
-                                   f"{c['max_new_tokens']} new tokens, <= {c['max_active']} leaves per tree",
-                       "decode_tokens": int(tokens), "trees_per_rank": c["prompts"],
-                       "leaves_per_tree_final": [len(x) for x in results],
+            "config": {"workload": f"BASELINE config {args.tree_config}: {arch} architecture, "
+                                   f"{c['prompts']} prompts x {c['prompt_len']} ids"
+                                   f"{' split across the ranks' if c['shard'] else ' per rank'}, "
+                                   f"{c['max_new_tokens']} new tokens, <= {M} leaves per tree",
+                       "decode_tokens": int(tokens), "trees_rank0": n_trees,
+                       "entropy_threshold_rank0": round(thr, 4),
+                       "leaves_per_tree_final_rank0": [min(leaves), float(np.mean(leaves)), max(leaves)],
                        "parallelism": f"independent trees x{world}"},
             "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
             "clocks": clk,
-            "note": "decode steps run as CUDA graphs; all trees of a rank advance in lockstep, one forward pass "
-                    "per step; the warm-up rollout captures the graphs",
+            "note": ("decode steps run as CUDA graphs" if c["graphs"] else
+                     "eager decode steps planned on the device (no per-layer host work)")
+                    + "; all trees of a rank advance in lockstep, one forward pass per step; branch threshold = "
+                      "90th percentile of a 32-step warm-up's gate entropies",
         }), flush=True)
     if world > 1:
         dist.barrier()

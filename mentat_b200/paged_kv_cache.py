@@ -364,16 +364,24 @@ class PagedKVCacheManager:
         """Host bookkeeping of one token appended to every layer of each sequence,
         for callers that append on the device without going through this class
         (a replayed CUDA graph of the decode step)."""
+        L, bs, cap = self.num_layers, self.block_size, self.max_blocks_per_seq
         for s in seq_ids:
             seq = self._sequences[s]
-            if len(set(seq.num_tokens)) == 1 and len(set(seq.num_blocks)) == 1:
-                self._mirror_append(seq, 0, 1)
-                n0, b0, t0 = seq.num_tokens[0], seq.num_blocks[0], seq.tokens_in_last_block[0]
-                seq.num_tokens[:] = [n0] * self.num_layers
-                seq.num_blocks[:] = [b0] * self.num_layers
-                seq.tokens_in_last_block[:] = [t0] * self.num_layers
+            nt, nb, tf = seq.num_tokens, seq.num_blocks, seq.tokens_in_last_block
+            n0, b0, t0 = nt[0], nb[0], tf[0]
+            if nt.count(n0) == L and nb.count(b0) == L and tf.count(t0) == L:
+                # every layer alike (the decode case): one token, inline
+                if b0 == 0 or t0 == bs:
+                    b0, t0 = b0 + 1, 1
+                    if b0 > cap:
+                        self._mirror_append(seq, 0, 1)  # raises the reference's error
+                else:
+                    t0 += 1
+                nt[:] = [n0 + 1] * L
+                nb[:] = [b0] * L
+                tf[:] = [t0] * L
             else:
-                for layer in range(self.num_layers):
+                for layer in range(L):
                     self._mirror_append(seq, layer, 1)
 
     def append_tokens(self, seq_id: int, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:

@@ -268,6 +268,15 @@ class PagedLM:
         self._graphs[N] = g
         return g
 
+    # Static eager decode: the graph path's forward run without capture, for
+    # batches whose many distinct sizes would each need a graph.  It plans
+    # from the device tables like a replay, so a step has no per-layer host work.
+    _static_max_len = None
+
+    def enable_static(self, max_len: int) -> None:
+        self._graph_max_len = max_len
+        self._static_max_len = max_len
+
     @torch.no_grad()
     def decode(self, tokens: torch.Tensor, seq_ids: list) -> tuple:
         """One token per sequence: logits (N, V) and final hidden states (N, D)."""
@@ -280,6 +289,10 @@ class PagedLM:
             self.graph_kernel_launches += g["kernels"]
             self.cache.mirror_decode_step(seq_ids)
             return g["logits"], g["hidden"]
+        if self._static_max_len is not None:
+            out = self._forward_static(tokens.view(N), self.cache._slots_dev(seq_ids))
+            self.cache.mirror_decode_step(seq_ids)
+            return out
         h = self.embed(tokens.view(N))
         pos = torch.tensor([self.cache.get_kv_length(s) for s in seq_ids], device=h.device).view(N, 1)
         cos, sin = self.rotary(h, pos)  # (N, 1, hd): broadcasts over heads
@@ -371,14 +384,15 @@ class TreeRollout:
                  block_size: int = 16, max_blocks: int = 8192, semantic_similarity_threshold: float = 0.85,
                  ema_alpha: float = 0.3, min_steps_before_prune: int = 5, soft_explore_window: int = 10,
                  soft_explore_initial: float = 0.3, max_seqs: int = 256, cuda_graphs: bool = True,
-                 max_prompt_len: int = 4096):
+                 max_prompt_len: int = 4096, entropy_threshold: Optional[float] = None,
+                 max_blocks_per_seq: Optional[int] = None, static_decode: bool = False):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
         hq = cfg.num_attention_heads
         hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // hq
         self.cache = PagedKVCacheManager(cfg.num_hidden_layers, cfg.num_key_value_heads, hd, max_blocks, block_size,
-                                         dev, dtype, max_seqs=max_seqs)
+                                         dev, dtype, max_seqs=max_seqs, max_blocks_per_seq=max_blocks_per_seq)
         self.lm = PagedLM(model, self.cache)
         self.eos = set(eos_token_id) if isinstance(eos_token_id, (list, tuple)) else {eos_token_id}
         self.M, self.K = max_active_branches, branching_factor
@@ -392,21 +406,43 @@ class TreeRollout:
                                    max_active_branches=max_active_branches, soft_explore_window=soft_explore_window)
         self.device = dev
         self.cuda_graphs = cuda_graphs
+        self.static_decode = static_decode  # without graphs: plan on the device, no per-layer host work
         self.max_prompt_len = max_prompt_len
+        # A fixed entropy threshold replaces the adaptive one in the branch test
+        # (the benchmark configurations calibrate it on a warm-up rollout); the
+        # room test M - n >= K stays.  entropy_log, when a list, collects every
+        # leaf's float-accurate gate entropy.
+        self.entropy_threshold = entropy_threshold
+        self.entropy_log = None
         self.decode_tokens = 0       # one per active leaf per decode step (step 0 excluded)
         self.decode_time_s = 0.0
         self.steps = 0
 
     # ---- per-leaf decision (generator.py:250-374) ---------------------------
-    def _apply(self, tree: Tree, leaf: Node, rec, step: int) -> None:
-        leaf.entropy_ema = float(rec["ema"])
-        if int(rec["branch"]):
-            kids = tree.branch(leaf, rec["topk_ids"][: self.K].tolist(), rec["topk_lps"][: self.K].tolist())
+    def _records(self, recs) -> list:
+        """The gate records of a step as plain tuples (ema, accurate entropy, branch,
+        argmax, argmax log-prob, top-K ids, top-K log-probs), one column at a time."""
+        K = self.K
+        return list(zip(recs["ema"].tolist(), recs["entropy_acc"].tolist(), recs["branch"].tolist(),
+                        recs["argmax"].tolist(), recs["argmax_lp"].tolist(), recs["topk_ids"][:, :K].tolist(),
+                        recs["topk_lps"][:, :K].tolist()))
+
+    def _apply(self, tree: Tree, leaf: Node, rec, step: int, n_active: int) -> None:
+        ema, h_acc, branch, arg, arg_lp, top_ids, top_lps = rec
+        leaf.entropy_ema = ema
+        if self.entropy_log is not None:
+            self.entropy_log.append(h_acc)
+        if self.entropy_threshold is not None:
+            # the fixed threshold is compared with the float-accurate entropy: the
+            # bf16-rounded one takes few distinct values (0.0625 apart near 11 nats)
+            branch = h_acc > self.entropy_threshold and self.M - n_active >= self.K
+        if branch:
+            kids = tree.branch(leaf, top_ids, top_lps)
             for c in kids:
                 c.creation_step = step
                 self._eos(c)
         else:
-            tree.extend(leaf, int(rec["argmax"]), float(rec["argmax_lp"]))
+            tree.extend(leaf, arg, arg_lp)
             self._eos(leaf)
 
     def _eos(self, node: Node) -> None:
@@ -474,15 +510,16 @@ class TreeRollout:
             tree.root.children[0] = first
             gate = Gate(self.device, self.gate_cfg)
             gate.launch(logits.view(1, -1), [[]], [None], num_active=1, step=0)
-            self._apply(tree, first, gate.result()[0], 0)
+            self._apply(tree, first, self._records(gate.result())[0], 0, 1)
             trees.append(tree)
             gates.append(gate)
+        longest = max(max(len(p) for p in prompts), self.max_prompt_len) + self.max_new_tokens + 1
         if self.cuda_graphs and self.lm._graphs is None:
-            longest = max(len(p) for p in prompts)
             # a step decodes at most every tree's live leaves, which stay within
             # max_active_branches + the K - 1 extra children of a last branch each
-            self.lm.enable_graphs(max(longest, self.max_prompt_len) + self.max_new_tokens + 1,
-                                  min(self.cache.max_seqs, len(prompts) * (self.M + self.K * self.M)))
+            self.lm.enable_graphs(longest, min(self.cache.max_seqs, len(prompts) * (self.M + self.K * self.M)))
+        elif self.static_decode and self.lm._graphs is None and self.lm._static_max_len is None:
+            self.lm.enable_static(longest)
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         for step in range(1, self.max_new_tokens):
@@ -496,20 +533,30 @@ class TreeRollout:
             logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])
             self.decode_tokens += len(leaves)
             self.sem.update(leaves, hidden, self.ema_alpha)                    # :376-398
-            # one gate launch per tree (its own active count), then one wait
-            a = 0
-            for lv, gate in zip(per_tree, gates):
-                if lv:
-                    gate.launch(logits[a:a + len(lv)], [lf.hist.view() for lf in lv],
-                                [lf.entropy_ema for lf in lv], num_active=len(lv), step=step)
-                a += len(lv)
-            for tree, lv, gate in zip(trees, per_tree, gates):
-                if not lv:
-                    continue
-                recs = gate.result()
-                for lf, rec in zip(lv, recs):
+            if self.entropy_threshold is None:
+                # adaptive threshold: one gate launch per tree (the threshold uses the
+                # tree's active count), then one wait
+                a = 0
+                for lv, gate in zip(per_tree, gates):
+                    if lv:
+                        gate.launch(logits[a:a + len(lv)], [lf.hist.view() for lf in lv],
+                                    [lf.entropy_ema for lf in lv], num_active=len(lv), step=step)
+                    a += len(lv)
+                recs_of = [self._records(gate.result()) if lv else None for lv, gate in zip(per_tree, gates)]
+            else:
+                # fixed threshold: the host takes the decision from the entropy, so one
+                # launch covers the leaves of every tree
+                gates[0].launch(logits[:len(leaves)], [lf.hist.view() for lf in leaves],
+                                [lf.entropy_ema for lf in leaves], num_active=len(leaves), step=step)
+                recs_all = self._records(gates[0].result())
+                recs_of, a = [], 0
+                for lv in per_tree:
+                    recs_of.append(recs_all[a:a + len(lv)])
+                    a += len(lv)
+            for tree, lv, recs in zip(trees, per_tree, recs_of):
+                for lf, rec in zip(lv, recs if lv else ()):
                     if lf.is_active:
-                        self._apply(tree, lf, rec, step)
+                        self._apply(tree, lf, rec, step, len(lv))
             self._prune_similar(trees, step)
         torch.cuda.synchronize(self.device)
         self.decode_time_s += time.perf_counter() - t0
@@ -524,6 +571,26 @@ class TreeRollout:
             res.sort(key=lambda r: r["norm_prob"], reverse=True)
             out.append(res)
         return out
+
+    def calibrate_threshold(self, prompts, steps: int = 32, q: float = 90.0) -> float:
+        """Sets the fixed entropy threshold to the q-th percentile of the gate
+        entropies of a ``steps``-step rollout of ``prompts`` without branching;
+        returns it.  The counters of that rollout are discarded."""
+        keep = (self.max_new_tokens, self.decode_tokens, self.decode_time_s, self.steps, self.cuda_graphs,
+                self.static_decode)
+        self.entropy_threshold, self.entropy_log = math.inf, []
+        # host-planned steps: graphs or the static path set up now would size their
+        # workspace for this short rollout
+        self.max_new_tokens, self.cuda_graphs, self.static_decode = steps + 1, False, False
+        try:
+            self.generate_many(prompts)
+            log = self.entropy_log[len(prompts):]  # the decode steps (step 0 is the prompt's own)
+        finally:
+            (self.max_new_tokens, self.decode_tokens, self.decode_time_s, self.steps, self.cuda_graphs,
+             self.static_decode) = keep
+            self.entropy_log = None
+        self.entropy_threshold = float(np.percentile(np.asarray(log, np.float64), q))
+        return self.entropy_threshold
 
     def tree_tokens_per_s(self) -> float:
         """Decode tokens per second of decode wall time (``generator.py:508-511``)."""
