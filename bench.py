@@ -173,6 +173,12 @@ TREE_CONFIGS = {
     3: dict(family="llama", vocab=128256, hidden=4096, intermediate=14336, layers=32, heads=32, kv_heads=8,
             head_dim=128, rope_theta=500000.0, prompts=64, prompt_len=2048, max_new_tokens=512, max_active=16,
             eos=128001, shard=True, graphs=False),
+    # Qwen3-32B architecture, random init, bf16; 32 prompts of 4096
+    # ids, trees of up to 32 leaves, 1024 new tokens; tensor parallel by KV head over
+    # the ranks (one KV head per GPU at 8), NCCL all-reduce after o_proj and down_proj
+    5: dict(family="qwen3", vocab=151936, hidden=5120, intermediate=25600, layers=64, heads=64, kv_heads=8,
+            head_dim=128, rope_theta=1000000.0, prompts=32, prompt_len=4096, max_new_tokens=1024, max_active=32,
+            eos=151645, shard=False, graphs=False, tp=True, tie=False, min_world=4),
 }
 
 
@@ -184,7 +190,7 @@ def tree_model(c, device, seed):
         cfg = Cfg(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
                   num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
                   head_dim=c["head_dim"], max_position_embeddings=40960, rms_norm_eps=1e-6,
-                  rope_theta=c["rope_theta"], tie_word_embeddings=True, eos_token_id=c["eos"])
+                  rope_theta=c["rope_theta"], tie_word_embeddings=c.get("tie", True), eos_token_id=c["eos"])
     else:
         from transformers import LlamaConfig as Cfg, LlamaForCausalLM as Model
         cfg = Cfg(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
@@ -219,8 +225,24 @@ def run_tree(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
     c = TREE_CONFIGS[args.tree_config]
+    tp = bool(c.get("tp"))
+    if world < c.get("min_world", 1):
+        if rank == 0:
+            print(json.dumps({"metric": f"tree tokens/s (config {args.tree_config})",
+                              "unavailable": f"needs >= {c['min_world']} GPUs (KV cache of the tree)"}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     model = tree_model(c, device, args.seed)
-    if c["shard"]:
+    if tp and world > 1:
+        from mentat_b200.tp import shard_model
+        full, model = model, shard_model(model, rank, world)
+        del full
+        torch.cuda.empty_cache()
+    if tp:  # every rank rolls out the same trees over its KV heads
+        rng = np.random.default_rng(args.seed * 1000)
+        prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
+    elif c["shard"]:
         rng = np.random.default_rng(args.seed * 1000)
         allp = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
         prompts = allp[rank::world]
@@ -236,7 +258,8 @@ def run_tree(args):
     r = TreeRollout(model, eos_token_id=c["eos"], max_active_branches=M, branching_factor=K,
                     max_new_tokens=c["max_new_tokens"], max_blocks=blocks, max_seqs=max_seqs,
                     cuda_graphs=c["graphs"], static_decode=not c["graphs"], max_prompt_len=c["prompt_len"],
-                    max_blocks_per_seq=-(-(c["prompt_len"] + c["max_new_tokens"]) // 16) + 2)
+                    max_blocks_per_seq=-(-(c["prompt_len"] + c["max_new_tokens"]) // 16) + 2,
+                    tp_group=dist.group.WORLD if tp and world > 1 else None)
     lib = _lib.load()
     thr = r.calibrate_threshold(prompts, steps=32, q=90.0)
     if c["graphs"]:
@@ -260,25 +283,27 @@ def run_tree(args):
     tok = torch.tensor([float(r.decode_tokens)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(tok, op=dist.ReduceOp.SUM)
+        if not tp:  # tensor parallel ranks decode the same tokens
+            dist.all_reduce(tok, op=dist.ReduceOp.SUM)
     secs, tokens = float(t.item()), float(tok.item())
     leaves = [len(x) for x in results]
     if rank == 0:
-        arch = {"qwen3": "Qwen3-0.6B", "llama": "Llama-3.1-8B"}[c["family"]]
+        arch = {2: "Qwen3-0.6B", 3: "Llama-3.1-8B", 5: "Qwen3-32B"}[args.tree_config]
         print(json.dumps({
             "metric": f"tree tokens/s (config {args.tree_config})", "value": round(tokens / secs, 2),
             "unit": "tokens/s", "n_gpus": world, "steps": r.steps, "warmup": 1,
             "ms_per_step": secs / max(r.steps, 1) * 1e3, "higher_is_better": True,
-            "scaling": "strong" if c["shard"] else "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if c["shard"] or tp else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, seeded uniform-random prompt ids)",
             "config": {"workload": f"BASELINE config {args.tree_config}: {arch} architecture, "
                                    f"{c['prompts']} prompts x {c['prompt_len']} ids"
-                                   f"{' split across the ranks' if c['shard'] else ' per rank'}, "
+                                   f"{' split across the ranks' if c['shard'] else (' on every rank' if tp else ' per rank')}, "
                                    f"{c['max_new_tokens']} new tokens, <= {M} leaves per tree",
                        "decode_tokens": int(tokens), "trees_rank0": n_trees,
                        "entropy_threshold_rank0": round(thr, 4),
                        "leaves_per_tree_final_rank0": [min(leaves), float(np.mean(leaves)), max(leaves)],
-                       "parallelism": f"independent trees x{world}"},
+                       "parallelism": (f"tensor parallel by KV head x{world} (NCCL all-reduce after o_proj "
+                                       f"and down_proj)" if tp and world > 1 else f"independent trees x{world}")},
             "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
             "clocks": clk,
             "note": ("decode steps run as CUDA graphs" if c["graphs"] else

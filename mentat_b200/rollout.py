@@ -16,7 +16,8 @@ drives its layers the way the reference's ``PagedModelWrapper`` and adapters
 do (``generator_utils.py:255-418``, ``adapters/qwen3_adapter.py``,
 ``adapters/llama_adapter.py``): pre-attention norm, q/k/v projections, QK-norm
 on Qwen3, rotate-half RoPE at the sequence's cached length, append, attention,
-o_proj, MLP, final norm and lm_head.
+o_proj, MLP, final norm and lm_head; under tensor parallelism by KV head
+(``tp.py``) the attention and MLP outputs are all-reduced over the group.
 
 ``TreeRollout.generate_many`` runs several trees in lockstep, one batched
 forward pass per step for the active leaves of all of them (the reference
@@ -174,15 +175,23 @@ class Tree:
 class PagedLM:
     """Runs a Hugging Face Qwen3 / Llama causal LM over the paged cache."""
 
-    def __init__(self, model, cache: PagedKVCacheManager):
+    def __init__(self, model, cache: PagedKVCacheManager, tp_group=None):
         base = model.model
         self.model, self.cache = model, cache
+        # tensor parallelism by KV head (``tp.shard_model``): the attention and MLP
+        # outputs are partial sums over the group, all-reduced before the residual
+        self.tp_group = tp_group
         self.embed, self.layers, self.norm, self.lm_head = base.embed_tokens, base.layers, base.norm, model.lm_head
         self.rotary = base.rotary_emb
         cfg = model.config
         self.hq, self.hkv = cfg.num_attention_heads, cfg.num_key_value_heads
         self.hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.hq
         self.qk_norm = hasattr(self.layers[0].self_attn, "q_norm")  # Qwen3
+
+    def _sum(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp_group is not None:
+            torch.distributed.all_reduce(x, group=self.tp_group)
+        return x
 
     @staticmethod
     def _rope(t, cos, sin):
@@ -211,8 +220,8 @@ class PagedLM:
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
             o = attn_prefill(q, k, v)
             self.cache.append_tokens(seq_id, layer_idx, k[0], v[0])
-            h = h + attn.o_proj(o.reshape(1, L, -1))
-            h = h + blk.mlp(blk.post_attention_layernorm(h))
+            h = h + self._sum(attn.o_proj(o.reshape(1, L, -1)))
+            h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         return self.lm_head(self.norm(h)[0, -1])
 
     # ---- CUDA-graph decode ----------------------------------------------------
@@ -247,8 +256,8 @@ class PagedLM:
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
             torch.ops.mentat_b200.append_batched(c._k_all, c._v_all, slots, k, v, c._op_id, layer_idx)
             o = torch.ops.mentat_b200.paged_decode(q, slots, self._graph_max_len, c._op_id, layer_idx, scale)
-            h = h + attn.o_proj(o.reshape(N, -1))
-            h = h + blk.mlp(blk.post_attention_layernorm(h))
+            h = h + self._sum(attn.o_proj(o.reshape(N, -1)))
+            h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         h = self.norm(h)
         return self.lm_head(h), h
 
@@ -304,8 +313,8 @@ class PagedLM:
             self.cache.append_tokens_batched(seq_ids, layer_idx, k, v)
             pk, pv, cu, mx = self.cache.build_packed_kv(seq_ids, layer_idx)
             o = attn_decode(q, pk, pv, None, cu, mx, N)
-            h = h + attn.o_proj(o.reshape(N, -1))
-            h = h + blk.mlp(blk.post_attention_layernorm(h))
+            h = h + self._sum(attn.o_proj(o.reshape(N, -1)))
+            h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         h = self.norm(h)
         return self.lm_head(h), h
 
@@ -385,7 +394,7 @@ class TreeRollout:
                  ema_alpha: float = 0.3, min_steps_before_prune: int = 5, soft_explore_window: int = 10,
                  soft_explore_initial: float = 0.3, max_seqs: int = 256, cuda_graphs: bool = True,
                  max_prompt_len: int = 4096, entropy_threshold: Optional[float] = None,
-                 max_blocks_per_seq: Optional[int] = None, static_decode: bool = False):
+                 max_blocks_per_seq: Optional[int] = None, static_decode: bool = False, tp_group=None):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -393,7 +402,7 @@ class TreeRollout:
         hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // hq
         self.cache = PagedKVCacheManager(cfg.num_hidden_layers, cfg.num_key_value_heads, hd, max_blocks, block_size,
                                          dev, dtype, max_seqs=max_seqs, max_blocks_per_seq=max_blocks_per_seq)
-        self.lm = PagedLM(model, self.cache)
+        self.lm = PagedLM(model, self.cache, tp_group)
         self.eos = set(eos_token_id) if isinstance(eos_token_id, (list, tuple)) else {eos_token_id}
         self.M, self.K = max_active_branches, branching_factor
         self.max_new_tokens = max_new_tokens
