@@ -603,101 +603,84 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// 3. merge
+// 3. merge: D/64 warps per (sequence, q head), each over 64 output dimensions
+//    (two per lane).  Lane p holds partial p's (m, l); a butterfly of
+//    log-sum-exp combines gives every lane the total (M, L), and lane p's weight
+//    2^(m_p - M) reaches the others by shuffle.  The first 16 partial rows are
+//    all requested before the part count is read; more are taken 16 at a time.
 // ---------------------------------------------------------------------------
-// One CTA per (sequence, q head).  The partials' (m, l) pairs are read in
-// parallel into shared memory, then every thread (one output element) sums
-// its column over the partials with independent loads.
-constexpr int MERGE_MAXP_SMEM = 1024;
+constexpr int MERGE_WARPS = 4;  // warps per CTA
+
 template <typename T, int D>
-__global__ void __launch_bounds__(D, 2048 / D) k_merge(mentat_kv_cache c, int Hq, DecodeWs ws, int max_parts,
-                                                       T* __restrict__ out, int64_t out_stride) {
-    constexpr int NW = D / 32;
-    constexpr int B = 12;  // partial rows loaded per batch
-    __shared__ float s_w[MERGE_MAXP_SMEM];
-    __shared__ float s_rm[NW], s_rl[NW];
-    __shared__ float s_ml[2];
+__global__ void __launch_bounds__(32 * MERGE_WARPS, 8) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
+                                                          int max_parts, T* __restrict__ out, int64_t out_stride) {
+    constexpr int WPP = D / 64;  // warps per (sequence, head)
+    constexpr int B = 16;        // partial rows in flight per lane (64 registers, no spills)
     griddep_wait();  // every unit kernel's partials
     griddep_launch();
     TL_FIRST(8);
-    const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
+    const int pair = gw / WPP, part = gw % WPP;
+    if (pair >= n * Hq) return;
+    const int i = pair / Hq, hq = pair % Hq;
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
     const int64_t pstride = (int64_t)Hq * 2;
-    const float* po = ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + d;
-    const int64_t ostride = (int64_t)Hq * D;
-    // the first batch of partial rows is loaded before the part count is known:
-    // rows up to max_parts exist in the workspace, and those past the count are
-    // masked below (their contents are never used)
-    float v[B];
+    const float2* po =
+        reinterpret_cast<const float2*>(ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + part * 64) + lane;
+    const int64_t ostride = (int64_t)Hq * D / 2;  // in float2
+    // rows up to max_parts exist in the workspace; those past the count get weight 0
+    float2 v[B];
 #pragma unroll
-    for (int j = 0; j < B; ++j) v[j] = j < max_parts ? po[j * ostride] : 0.f;
+    for (int j = 0; j < B; ++j)
+        if (j < max_parts) v[j] = po[j * ostride];
     const int P = ws.nparts[i];
     // a tensor-core unit kernel that gave up a bounded wait left partials unwritten
     const bool aborted = ws.hdr[HDR_TC_ABORT] != 0;
-    if (aborted && i == 0 && hq == 0 && d == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
-    // (m, l) of all partials combined: (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
+    if (aborted && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
+    // (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
     auto comb = [](float& m, float& l, float m2, float l2) {
         const float mn = fmaxf(m, m2);
         l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (m2 == -INFINITY ? 0.f : l2 * exp2f(m2 - mn));
         m = mn;
     };
-    if (P <= 32) {  // one warp
-        if (warp == 0) {
-            float m = -INFINITY, l = 0.f;
-            if (lane < P) {
-                const float2 x = *reinterpret_cast<const float2*>(ml + lane * pstride);
-                m = x.x;
-                l = x.y;
-            }
-            const float mp = m;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) comb(m, l, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, l, o));
-            if (lane < P) s_w[lane] = exp2f(mp - m);
-            if (lane == 0) {
-                s_ml[0] = m;
-                s_ml[1] = l;
-            }
-        }
-    } else {
+    float M = -INFINITY, L = 0.f;
+    for (int p0 = 0; p0 < P; p0 += 32) {
         float m = -INFINITY, l = 0.f;
-        for (int p = d; p < P; p += D) {
-            const float2 x = *reinterpret_cast<const float2*>(ml + p * pstride);
-            comb(m, l, x.x, x.y);
+        if (p0 + lane < P) {
+            const float2 x = *reinterpret_cast<const float2*>(ml + (p0 + lane) * pstride);
+            m = x.x;
+            l = x.y;
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) comb(m, l, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, l, o));
-        if (lane == 0) {
-            s_rm[warp] = m;
-            s_rl[warp] = l;
-        }
-        __syncthreads();
-        if (d == 0) {
-            float mm = s_rm[0], ll = s_rl[0];
-            for (int w2 = 1; w2 < NW; ++w2) comb(mm, ll, s_rm[w2], s_rl[w2]);
-            s_ml[0] = mm;
-            s_ml[1] = ll;
-        }
-        __syncthreads();
-        const float mm = s_ml[0];
-        for (int p = d; p < P && p < MERGE_MAXP_SMEM; p += D) s_w[p] = exp2f(ml[p * pstride] - mm);
+        comb(M, L, m, l);
     }
-    __syncthreads();
-    const float m = s_ml[0], l = s_ml[1];
-    auto weight = [&](int p) { return p < MERGE_MAXP_SMEM ? s_w[p] : exp2f(ml[p * pstride] - m); };
-    float acc0 = 0.f, acc1 = 0.f;
+    float a0 = 0.f, a1 = 0.f;
+    for (int b0 = 0; b0 < P; b0 += B) {
+        if (b0 > 0) {  // rows after the first batch
 #pragma unroll
-    for (int j = 0; j < B; ++j)
-        if (j < P) (j & 1 ? acc1 : acc0) += v[j] * weight(j);
-    for (int p0 = B; p0 < P; p0 += B) {
+            for (int j = 0; j < B; ++j)
+                if (b0 + j < P) v[j] = po[(int64_t)(b0 + j) * ostride];
+        }
+        // weights of rows b0 .. b0 + B - 1: lane k holds row (b0 & ~31) + k's
+        const int w0 = b0 & ~31;
+        const float wlo = w0 + lane < P ? exp2f(ml[(w0 + lane) * pstride] - M) : 0.f;
+        const float whi = w0 + 32 + lane < P ? exp2f(ml[(w0 + 32 + lane) * pstride] - M) : 0.f;
 #pragma unroll
-        for (int j = 0; j < B; ++j) v[j] = p0 + j < P ? po[(p0 + j) * ostride] : 0.f;
-#pragma unroll
-        for (int j = 0; j < B; ++j)
-            if (p0 + j < P) (j & 1 ? acc1 : acc0) += v[j] * weight(p0 + j);
+        for (int j = 0; j < B; ++j) {
+            const int r = b0 + j - w0;  // < 64: b0 is a multiple of B, w0 = b0 rounded down to 32
+            const float wj = __shfl_sync(0xffffffffu, r < 32 ? wlo : whi, r & 31);
+            if (b0 + j < P) {
+                a0 = fmaf(v[j].x, wj, a0);
+                a1 = fmaf(v[j].y, wj, a1);
+            }
+        }
     }
-    const float o = acc0 + acc1;
-    const float r = (P > 0 && l > 0.f && !aborted) ? o / l : 0.f;
-    out[(int64_t)i * out_stride + (int64_t)hq * D + d] = Elem<T>::from_f(r);
+    const bool ok = P > 0 && L > 0.f && !aborted;
+    T* dst = out + (int64_t)i * out_stride + (int64_t)hq * D + part * 64 + lane * 2;
+    dst[0] = Elem<T>::from_f(ok ? a0 / L : 0.f);
+    dst[1] = Elem<T>::from_f(ok ? a1 / L : 0.f);
     TL_LAST(9);
 }
 
@@ -852,8 +835,8 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
         }
     }
     prof_mark(4, s);
-    if (launch(pdl, k_merge<T, D>, dim3(n, Hq), dim3(D), 0, s, *c, Hq, ws, max_parts, reinterpret_cast<T*>(out),
-               out_stride) != cudaSuccess)
+    if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
+               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     prof_mark(5, s);
