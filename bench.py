@@ -317,11 +317,12 @@ def run_tree(args):
 
 
 def run_profile_kernels(args):
-    """The gate and the append kernels on benchmark-sized inputs, for a profiler
-    capture: the gate over 32 leaves x 151936 bf16 logits (config 2's vocabulary)
-    with 200-token histories, and one-token batched appends to the 64 branches of
-    the config-4 tree (the first append after the forks copies every branch's
-    partial tail block).  Prints time per call and algorithmic GB/s."""
+    """The gate, append, fork / free and FFMA decode kernels on benchmark-sized
+    inputs, for a profiler capture: the gate over 32 leaves x 151936 bf16 logits
+    (config 2's vocabulary) with 200-token histories; one-token batched appends to
+    the 64 branches of the config-4 tree (the first append after the forks copies
+    every branch's partial tail block); fork + free of one of its branches; and
+    config 1's fp32 decode.  Prints time per call and algorithmic GB/s."""
     from mentat_b200.gate import GATE_OUT_DTYPE, Gate, GateConfig
     device = torch.device("cuda", 0)
     steps = max(args.steps, 1)
@@ -376,7 +377,44 @@ def run_profile_kernels(args):
     nb = NBR * HKV * D * 2 * ELEM
     print(f"append: {NBR} sequences x 1 token, {ms * 1e3:.1f} us/call, {nb / ms / 1e6:.2f} GB/s of K/V rows",
           flush=True)
+    # fork + free of one branch of the config-4 tree (k_fork refs its 2,000+ blocks,
+    # k_free releases them)
+    e0.record()
+    for _ in range(steps):
+        m.free_sequence(m.fork_sequence(kids[0]))
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"fork+free: one branch of {m.get_kv_length(kids[0])} tokens, "
+          f"{e0.elapsed_time(e1) / steps * 1e3:.1f} us per pair", flush=True)
     m.check()
+    del m
+    # BASELINE config 1 in fp32 (the FFMA unit kernel): Hq 16, Hkv 8, D 128, block 16,
+    # 8 branches sharing a 512-token prefix, 64 tokens of their own each
+    from mentat_b200 import PagedKVCacheManager
+    from mentat_b200.attention_backend import attn_decode
+    m1 = PagedKVCacheManager(1, 8, 128, max_blocks=1024, block_size=16, device=device, dtype=torch.float32,
+                             max_seqs=16)
+    kv = lambda n: torch.randn((n, 8, 128), generator=g, device=device)  # noqa: E731
+    root = m1.allocate_sequence()
+    m1.append_tokens(root, 0, kv(512), kv(512))
+    br = [m1.fork_sequence(root) for _ in range(8)]
+    m1.free_sequence(root)
+    for b in br:
+        m1.append_tokens(b, 0, kv(64), kv(64))
+    q1 = torch.randn((8, 16, 128), generator=g, device=device)
+    k1, v1, cu1, mx1 = m1.build_packed_kv(br, 0)
+    for _ in range(args.warmup):
+        attn_decode(q1, k1, v1, None, cu1, mx1, 8)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        attn_decode(q1, k1, v1, None, cu1, mx1, 8)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ub = 1024 * 8 * 128 * 2 * 4  # 512 + 8 x 64 distinct tokens
+    print(f"config 1 (fp32): {ms * 1e3:.1f} us/call, {ub / ms / 1e6:.1f} GB/s unique KV", flush=True)
+    m1.check()
 
 
 def run_profile_case(args):
@@ -526,11 +564,22 @@ def run_mentat(args):
     kv_host = torch.randn((args.steps + args.warmup, 2, NBR, HKV, D), generator=g).to(torch.bfloat16).pin_memory()
     out_host = torch.empty((NBR, HQ, D), dtype=torch.bfloat16).pin_memory()
 
+    # q goes up on a copy stream while the main stream appends the step's K/V rows
+    # (the attention waits for both); each step still starts after the previous
+    # step's work on the main stream, and the result comes back every step
+    copy_stream = torch.cuda.Stream(device)
+
     def e2e_step(i):
-        qd = q_host.to(device, non_blocking=True)
+        main = torch.cuda.current_stream(device)
+        copy_stream.wait_stream(main)
+        with torch.cuda.stream(copy_stream):
+            qd = q_host.to(device, non_blocking=True)
+        q_ready = copy_stream.record_event()
         kvd = kv_host[i].to(device, non_blocking=True)
         m.append_tokens_batched(kids, 0, kvd[0], kvd[1])
         kk, vv, cuk, mxk = m.build_packed_kv(kids, 0)
+        main.wait_event(q_ready)
+        qd.record_stream(main)
         o = attn_decode(qd, kk, vv, None, cuk, mxk, NBR)
         out_host.copy_(o, non_blocking=True)
 
@@ -598,8 +647,8 @@ def run_mentat(args):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(q_host.numel() * 2 + kv_host[0].numel() * 2),
                     "d2h_bytes_per_step": int(out_host.numel() * 2),
-                    "path": "pinned H2D q + new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
-                            "D2H output"},
+                    "path": "pinned H2D new K/V -> append_tokens_batched -> build_packed_kv -> attn_decode -> "
+                            "D2H output, with the pinned H2D of q on a copy stream beside the append"},
             "gpu_launches": int(launches),  # counted by the library over the device-timed loop
             "clocks": clk,
         }
