@@ -529,22 +529,49 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
         for (int t0 = t0u; t0 < t1u; t0 += TT) {
             const int cnt = min(TT, t1u - t0);
             __syncthreads();
-            for (int idx = tid; idx < cnt * D; idx += UNIT_THREADS) {
-                const int j = idx / D, d = idx % D;
-                const int p = t0 + j;
-                const int64_t off = pool_row(c, layer, tab[p / bs], p % bs) + (int64_t)head * D + d;
-                k_s[j][d] = Elem<T>::to_f(kpool[off]);
-                v_s[j][d] = Elem<T>::to_f(vpool[off]);
+            {  // K and V rows of the tile: 16-byte loads, all of a thread's in flight together
+                constexpr int VEC = 16 / sizeof(T);                      // elements per load
+                constexpr int PER = (TT * D / VEC + UNIT_THREADS - 1) / UNIT_THREADS;
+                uint4 kr[PER], vr[PER];
+#pragma unroll
+                for (int k = 0; k < PER; ++k) {
+                    const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
+                    if (j < cnt) {
+                        const int p = t0 + j;
+                        const int64_t off = pool_row(c, layer, tab[p / bs], p % bs) + (int64_t)head * D + d;
+                        kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
+                        vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < PER; ++k) {
+                    const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
+                    if (j < cnt) {
+                        const T* ke = reinterpret_cast<const T*>(&kr[k]);
+                        const T* ve = reinterpret_cast<const T*>(&vr[k]);
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) {
+                            k_s[j][d + e] = Elem<T>::to_f(ke[e]);
+                            v_s[j][d + e] = Elem<T>::to_f(ve[e]);
+                        }
+                    }
+                }
             }
             __syncthreads();
             {  // scores: lane = token, warps stride the rows
                 const int j = lane;
                 for (int r = warp; r < R; r += UNIT_THREADS / 32) {
                     float s = -INFINITY;
-                    if (j < cnt) {
-                        s = 0.f;
+                    if (j < cnt) {  // four independent partial sums over the head dimension
+                        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 8
-                        for (int d = 0; d < D; ++d) s = fmaf(q_s[r][d], k_s[j][d], s);
+                        for (int d = 0; d < D; d += 4) {
+                            s0 = fmaf(q_s[r][d], k_s[j][d], s0);
+                            s1 = fmaf(q_s[r][d + 1], k_s[j][d + 1], s1);
+                            s2 = fmaf(q_s[r][d + 2], k_s[j][d + 2], s2);
+                            s3 = fmaf(q_s[r][d + 3], k_s[j][d + 3], s3);
+                        }
+                        s = (s0 + s1) + (s2 + s3);
                     }
                     float mx = s;
 #pragma unroll
