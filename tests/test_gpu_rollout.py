@@ -24,11 +24,11 @@ pytestmark = pytest.mark.gpu
 GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "rollout.json")))
 
 
-def _rollout(c, model):
+def _rollout(c, model, **kw):
     from mentat_b200.rollout import TreeRollout
     return TreeRollout(model, eos_token_id=c["eos"], max_active_branches=c["max_active_branches"],
                        branching_factor=c["branching_factor"], max_new_tokens=c["max_new_tokens"], block_size=16,
-                       max_blocks=4096)
+                       max_blocks=4096, **kw)
 
 
 def _check(name, got, want, tag):
@@ -53,3 +53,49 @@ def test_rollout_matches_reference_generator(name):
     for i, got in enumerate(r.generate_many(prompts)):
         _check(name, got, GOLDEN[name][i], f"lockstep prompt {i}")
     assert r.decode_tokens == sum(g["decode_tokens_total"] for g in GOLDEN[name])
+
+
+@pytest.mark.parametrize("name", sorted(ROLLOUT_CASES))
+def test_static_decode_matches_reference_generator(name):
+    """The eager device-planned step (no graphs) gives the reference's trees too."""
+    c = ROLLOUT_CASES[name]
+    model = rollout_model(c, device="cuda")
+    r = _rollout(c, model, cuda_graphs=False, static_decode=True)
+    for i, got in enumerate(r.generate_many(rollout_prompts(c))):
+        _check(name, got, GOLDEN[name][i], f"static prompt {i}")
+
+
+def test_fixed_threshold_extremes():
+    """An infinite threshold never branches (one leaf per tree, one token per
+    step); a threshold below every entropy branches at the first step, as far
+    as the room test M - n >= K allows."""
+    import math
+    c = ROLLOUT_CASES["qwen3_fp32"]
+    model = rollout_model(c, device="cuda")
+    prompts = rollout_prompts(c)
+    r = _rollout(c, model, entropy_threshold=math.inf)
+    res = r.generate_many(prompts)
+    assert [len(x) for x in res] == [1] * len(prompts)
+    assert all(len(x[0]["token_ids"]) <= c["max_new_tokens"] for x in res)
+    r = _rollout(c, model, entropy_threshold=-math.inf)
+    res = r.generate_many(prompts)
+    assert all(len(x) >= c["branching_factor"] for x in res)
+    assert all(len(x) <= c["max_active_branches"] + c["branching_factor"] - 1 for x in res)
+
+
+def test_calibrated_threshold_is_the_warmup_percentile():
+    import numpy as np_
+    c = ROLLOUT_CASES["llama_fp32"]
+    model = rollout_model(c, device="cuda")
+    prompts = rollout_prompts(c)
+    r = _rollout(c, model)
+    r.entropy_log = []
+    keep = r.max_new_tokens
+    r.entropy_threshold = float("inf")
+    r.max_new_tokens = 9
+    r.generate_many(prompts)
+    want = float(np_.percentile(np_.asarray(r.entropy_log[len(prompts):]), 75.0))
+    r.entropy_log, r.entropy_threshold, r.max_new_tokens = None, None, keep
+    thr = r.calibrate_threshold(prompts, steps=8, q=75.0)
+    assert thr == want
+    assert r.entropy_threshold == thr and r.max_new_tokens == keep and r.decode_tokens == 8 * len(prompts)
