@@ -767,33 +767,10 @@ static bool narrow_enabled() {
     return v != 0;
 }
 
-// Decode kernels go out with programmatic stream serialization: each may be
-// scheduled while its predecessor on the stream runs, and waits for it with
-// griddep_wait (the narrow kernel waits for the wide one only at its end).
-// MENTAT_PDL=0 launches them one after another instead.
-static bool pdl_enabled() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("MENTAT_PDL");
-        v = (e && *e) ? (atoi(e) != 0) : 1;
-    }
-    return v != 0;
-}
-template <typename... KArgs, typename... Args>
-static cudaError_t launch(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                          Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-}
+// Decode kernels go out with programmatic stream serialization (pdl_enabled,
+// launch in common.cuh): each may be scheduled while its predecessor on the
+// stream runs, and waits for it with griddep_wait (the narrow kernel waits for
+// the wide one only at its end).
 
 template <typename T, int D>
 static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,

@@ -202,6 +202,8 @@ __global__ void __launch_bounds__(1024) k_append_plan(mentat_kv_cache c, int lay
     __shared__ int smem32[32];
     __shared__ int s_abort;
     __shared__ long long s_head;
+    griddep_wait();  // the stream's previous work (tables, lengths, slots)
+    griddep_launch();
     AppendScratch sc(c);
     if (threadIdx.x == 0) s_abort = has_error(c) ? 1 : 0;
     __syncthreads();
@@ -301,6 +303,8 @@ __global__ void __launch_bounds__(1024) k_append_plan(mentat_kv_cache c, int lay
 // data movement of the batched append: CoW copy of the whole block, then the token row
 __global__ void k_append_data(mentat_kv_cache c, int layer, int n, const uint8_t* k, int64_t k_sb,
                               const uint8_t* v, int64_t v_sb) {
+    griddep_wait();  // the plan's scratch (and, through it, the K/V rows' producers)
+    griddep_launch();
     AppendScratch sc(c);
     const int mode = sc.mode[0];
     if (mode == 2) return;
@@ -601,10 +605,16 @@ int mentat_kv_append_batched(const mentat_kv_cache* c, int32_t layer, const int3
     if (n == 0) return MENTAT_OK;
     const int esz = dtype_bytes(c->dtype);
     int threads = ((n + 31) / 32) * 32;
-    k_append_plan<<<1, threads, 2 * n * sizeof(int), s>>>(*c, layer, slots, n);
+    // both go out with programmatic stream serialization, so their launches overlap
+    // the work ahead of them; each waits for its predecessor before touching memory
+    const bool pdl = pdl_enabled();
+    if (launch(pdl, k_append_plan, dim3(1), dim3(threads), 2 * n * sizeof(int), s, *c, layer, slots, n) !=
+        cudaSuccess)
+        return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
-    k_append_data<<<n, 128, 0, s>>>(*c, layer, n, (const uint8_t*)k, k_stride * esz, (const uint8_t*)v,
-                                    v_stride * esz);
+    if (launch(pdl, k_append_data, dim3(n), dim3(128), 0, s, *c, layer, n, (const uint8_t*)k, k_stride * esz,
+               (const uint8_t*)v, v_stride * esz) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     return MENTAT_OK;
 }
