@@ -172,7 +172,7 @@ TREE_CONFIGS = {
     # across the ranks (strong scaling)
     3: dict(family="llama", vocab=128256, hidden=4096, intermediate=14336, layers=32, heads=32, kv_heads=8,
             head_dim=128, rope_theta=500000.0, prompts=64, prompt_len=2048, max_new_tokens=512, max_active=16,
-            eos=128001, shard=True, graphs=False),
+            eos=128001, shard=True, graphs=True, bucket=64),
     # Qwen3-32B architecture, random init, bf16; 32 prompts of 4096
     # ids, trees of up to 32 leaves, 1024 new tokens; tensor parallel by KV head over
     # the ranks (one KV head per GPU at 8), NCCL all-reduce after o_proj and down_proj
@@ -252,18 +252,19 @@ def run_tree(args):
     M, K = c["max_active"], 3
     n_trees = len(prompts)
     # every live leaf of every tree at once, plus the children of one step's branches
-    max_seqs = n_trees * (M + K) + 16
+    max_seqs = n_trees * (M + K) + 16 + c.get("bucket", 0)  # + the padding of the last graph bucket
     # a tree's prompt blocks are shared; each live leaf owns at most its generated blocks + a CoW'd tail
     blocks = n_trees * (-(-c["prompt_len"] // 16) + (M + K) * (-(-c["max_new_tokens"] // 16) + 2)) + 64
     r = TreeRollout(model, eos_token_id=c["eos"], max_active_branches=M, branching_factor=K,
                     max_new_tokens=c["max_new_tokens"], max_blocks=blocks, max_seqs=max_seqs,
-                    cuda_graphs=c["graphs"], static_decode=not c["graphs"], max_prompt_len=c["prompt_len"],
+                    cuda_graphs=c["graphs"], static_decode=not c["graphs"], graph_bucket=c.get("bucket"),
+                    max_prompt_len=c["prompt_len"],
                     max_blocks_per_seq=-(-(c["prompt_len"] + c["max_new_tokens"]) // 16) + 2,
                     tp_group=dist.group.WORLD if tp and world > 1 else None)
     lib = _lib.load()
     thr = r.calibrate_threshold(prompts, steps=32, q=90.0)
     if c["graphs"]:
-        r.generate_many(prompts)  # warm-up: captures the decode graphs
+        r.generate_many(prompts)  # warm-up: captures the decode graphs (one per bucket of leaf counts)
     else:
         full = r.max_new_tokens
         r.max_new_tokens = 16     # warm-up of the eager path
@@ -306,7 +307,8 @@ def run_tree(args):
                                        f"and down_proj)" if tp and world > 1 else f"independent trees x{world}")},
             "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
             "clocks": clk,
-            "note": ("decode steps run as CUDA graphs" if c["graphs"] else
+            "note": (("decode steps run as CUDA graphs" + (f" (leaf counts padded to multiples of {c['bucket']})"
+                                                           if c.get("bucket") else "")) if c["graphs"] else
                      "eager decode steps planned on the device (no per-layer host work)")
                     + "; all trees of a rank advance in lockstep, one forward pass per step; branch threshold = "
                       "90th percentile of a 32-step warm-up's gate entropies",

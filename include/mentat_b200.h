@@ -105,7 +105,8 @@ int mentat_kv_free(const mentat_kv_cache* c, int32_t slot, int32_t max_nblocks, 
  * sequences (slots, device int32[n]) in layer `layer`: new block when the tail
  * is full or the table empty, copy-on-write of a shared tail, then the scatter
  * of k/v rows ([n][num_kv_heads][head_dim], token stride k_stride/v_stride in
- * elements).  n <= 1024 per call. */
+ * elements).  n <= 1024 per call.  An entry whose slot is -1 is skipped (padding
+ * of a batch to a fixed size, e.g. a captured CUDA graph's). */
 int mentat_kv_append_batched(const mentat_kv_cache* c, int32_t layer, const int32_t* slots,
                              int32_t n, const void* k, int64_t k_stride, const void* v,
                              int64_t v_stride, cudaStream_t s);

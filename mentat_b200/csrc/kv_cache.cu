@@ -213,7 +213,13 @@ __global__ void __launch_bounds__(1024) k_append_plan(mentat_kv_cache c, int lay
     }
     const int i = threadIdx.x;
     int slot = -1, nb = 0, tf = 0, tblk = -1;
-    const bool valid = i < n;
+    // slot -1 marks a padding entry (a batch padded to a captured size): skipped
+    const bool valid = i < n && slots[i] != -1;
+    if (i < n && !valid) {
+        s_slot[i] = -1;
+        s_tblk[i] = -1;
+        sc.dst_blk[i] = -1;
+    }
     if (valid) {
         slot = slots[i];
         if (slot < 0 || slot >= c.max_seqs) {
@@ -237,7 +243,8 @@ __global__ void __launch_bounds__(1024) k_append_plan(mentat_kv_cache c, int lay
         if (threadIdx.x == 0) {
             sc.mode[0] = 1;
             if (dup == 1)
-                for (int k = 0; k < n && !has_error(c); ++k) append_one_seq(c, layer, s_slot[k], sc, k);
+                for (int k = 0; k < n && !has_error(c); ++k)
+                    if (s_slot[k] >= 0) append_one_seq(c, layer, s_slot[k], sc, k);
             if (has_error(c)) sc.mode[0] = 2;
         }
         return;
@@ -321,6 +328,7 @@ __global__ void k_append_data(mentat_kv_cache c, int layer, int n, const uint8_t
     }
     for (int i = lo; i < hi; ++i) {
         const int dst = sc.dst_blk[i], slot = sc.dst_slot[i], src = sc.cow_src[i];
+        if (dst < 0) continue;  // padding entry (uniform across the CTA)
         if (src >= 0) {
             block_copy_bytes(kp + pool_row(c, layer, dst, 0) * esz, kp + pool_row(c, layer, src, 0) * esz, blk_bytes);
             block_copy_bytes(vp + pool_row(c, layer, dst, 0) * esz, vp + pool_row(c, layer, src, 0) * esz, blk_bytes);

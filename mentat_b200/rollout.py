@@ -233,21 +233,37 @@ class PagedLM:
     # needs no host work beyond the host mirror of the lengths.
     _graphs = None
 
-    def enable_graphs(self, max_len: int, max_n: int) -> None:
+    def enable_graphs(self, max_len: int, max_n: int, bucket: Optional[int] = None) -> None:
         """Decode through CUDA graphs; ``max_len`` bounds every sequence's length
         and ``max_n`` the sequences of one step (they size the shared workspace,
-        which captured graphs must not see reallocated)."""
+        which captured graphs must not see reallocated).  With ``bucket``, a step
+        of N sequences replays the graph of N rounded up to a multiple of
+        ``bucket``: the extra rows append nothing (slot -1) and attend over an
+        empty sequence, so a few graphs cover every leaf count."""
+        self._bucket = bucket
+        if bucket:
+            max_n = -(-max_n // bucket) * bucket
+            if self._pad_seq is None:
+                self._pad_seq = self.cache.allocate_sequence()  # never appended to: length 0
         self.cache.decode_workspace(max_n, self.hq, max_len)
         self._graph_max_len = max_len
         self._graph_max_n = max_n
         self._graphs = {}
         self._pool = torch.cuda.graph_pool_handle()
 
-    def _forward_static(self, tokens: torch.Tensor, slots: torch.Tensor) -> tuple:
+    _bucket = None
+    _pad_seq = None
+
+    def _forward_static(self, tokens: torch.Tensor, slots: torch.Tensor,
+                        dec_slots: Optional[torch.Tensor] = None) -> tuple:
+        """One decode step over static buffers; ``slots`` receive the new K/V rows,
+        ``dec_slots`` (default ``slots``) are the sequences attended over."""
         c = self.cache
         N = tokens.shape[0]
+        if dec_slots is None:
+            dec_slots = slots
         h = self.embed(tokens)
-        pos = c._ntok[0].index_select(0, slots).to(torch.long).view(N, 1)  # lengths before this token
+        pos = c._ntok[0].index_select(0, dec_slots).to(torch.long).view(N, 1)  # lengths before this token
         cos, sin = self.rotary(h, pos)
         scale = 1.0 / (self.hd ** 0.5)
         for layer_idx, blk in enumerate(self.layers):
@@ -255,7 +271,7 @@ class PagedLM:
             q, k, v = self._qkv(attn, blk.input_layernorm(h), (N,))
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
             torch.ops.mentat_b200.append_batched(c._k_all, c._v_all, slots, k, v, c._op_id, layer_idx)
-            o = torch.ops.mentat_b200.paged_decode(q, slots, self._graph_max_len, c._op_id, layer_idx, scale)
+            o = torch.ops.mentat_b200.paged_decode(q, dec_slots, self._graph_max_len, c._op_id, layer_idx, scale)
             h = h + self._sum(attn.o_proj(o.reshape(N, -1)))
             h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         h = self.norm(h)
@@ -266,13 +282,17 @@ class PagedLM:
     graph_kernel_launches = 0
 
     def _capture(self, N: int) -> dict:
-        g = {"tokens": torch.zeros(N, dtype=torch.long, device=self.cache.device),
-             "slots": torch.zeros(N, dtype=torch.int32, device=self.cache.device),
+        dev = self.cache.device
+        g = {"tokens": torch.zeros(N, dtype=torch.long, device=dev),
+             "slots": torch.full((N,), -1, dtype=torch.int32, device=dev),
+             "dec_slots": torch.zeros(N, dtype=torch.int32, device=dev) if self._bucket else None,
              "graph": torch.cuda.CUDAGraph()}
+        if self._bucket:
+            g["dec_slots"].fill_(self.cache._sequences[self._pad_seq].slot)
         lib = _lib.load()
         n0 = lib.mentat_kernel_launch_count()
         with torch.cuda.graph(g["graph"], pool=self._pool):
-            g["logits"], g["hidden"] = self._forward_static(g["tokens"], g["slots"])
+            g["logits"], g["hidden"] = self._forward_static(g["tokens"], g["slots"], g["dec_slots"])
         g["kernels"] = lib.mentat_kernel_launch_count() - n0
         self._graphs[N] = g
         return g
@@ -291,13 +311,27 @@ class PagedLM:
         """One token per sequence: logits (N, V) and final hidden states (N, D)."""
         N = len(seq_ids)
         if self._graphs is not None and N <= self._graph_max_n:
-            g = self._graphs.get(N) or self._capture(N)
-            g["tokens"].copy_(tokens.view(N))
-            g["slots"].copy_(self.cache._slots_dev(seq_ids))
+            if self._bucket:
+                Nb = -(-N // self._bucket) * self._bucket
+                g = self._graphs.get(Nb) or self._capture(Nb)
+                # the padding rows: token 0, no append (slot -1), attention over the empty sequence
+                seq = self.cache._sequences
+                pad = seq[self._pad_seq].slot
+                sl = [seq[s].slot for s in seq_ids]
+                both = torch.tensor([sl + [-1] * (Nb - N), sl + [pad] * (Nb - N)], dtype=torch.int32)
+                up = self.cache._uploads.upload(both.view(-1)).view(2, Nb)
+                g["tokens"][:N].copy_(tokens.view(N))
+                g["tokens"][N:].zero_()
+                g["slots"].copy_(up[0])
+                g["dec_slots"].copy_(up[1])
+            else:
+                g = self._graphs.get(N) or self._capture(N)
+                g["tokens"].copy_(tokens.view(N))
+                g["slots"].copy_(self.cache._slots_dev(seq_ids))
             g["graph"].replay()
             self.graph_kernel_launches += g["kernels"]
             self.cache.mirror_decode_step(seq_ids)
-            return g["logits"], g["hidden"]
+            return g["logits"][:N], g["hidden"][:N]
         if self._static_max_len is not None:
             out = self._forward_static(tokens.view(N), self.cache._slots_dev(seq_ids))
             self.cache.mirror_decode_step(seq_ids)
@@ -394,7 +428,8 @@ class TreeRollout:
                  ema_alpha: float = 0.3, min_steps_before_prune: int = 5, soft_explore_window: int = 10,
                  soft_explore_initial: float = 0.3, max_seqs: int = 256, cuda_graphs: bool = True,
                  max_prompt_len: int = 4096, entropy_threshold: Optional[float] = None,
-                 max_blocks_per_seq: Optional[int] = None, static_decode: bool = False, tp_group=None):
+                 max_blocks_per_seq: Optional[int] = None, static_decode: bool = False, tp_group=None,
+                 graph_bucket: Optional[int] = None):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -416,6 +451,7 @@ class TreeRollout:
         self.device = dev
         self.cuda_graphs = cuda_graphs
         self.static_decode = static_decode  # without graphs: plan on the device, no per-layer host work
+        self.graph_bucket = graph_bucket    # graphs for leaf counts rounded up to a multiple of this
         self.max_prompt_len = max_prompt_len
         # A fixed entropy threshold replaces the adaptive one in the branch test
         # (the benchmark configurations calibrate it on a warm-up rollout); the
@@ -526,7 +562,8 @@ class TreeRollout:
         if self.cuda_graphs and self.lm._graphs is None:
             # a step decodes at most every tree's live leaves, which stay within
             # max_active_branches + the K - 1 extra children of a last branch each
-            self.lm.enable_graphs(longest, min(self.cache.max_seqs, len(prompts) * (self.M + self.K * self.M)))
+            self.lm.enable_graphs(longest, min(self.cache.max_seqs - 1, len(prompts) * (self.M + self.K * self.M)),
+                                  self.graph_bucket)
         elif self.static_decode and self.lm._graphs is None and self.lm._static_max_len is None:
             self.lm.enable_static(longest)
         torch.cuda.synchronize(self.device)

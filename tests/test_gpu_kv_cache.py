@@ -172,3 +172,35 @@ def test_out_of_blocks_raises_reference_message():
     s = m2.allocate_sequence()
     with pytest.raises(RuntimeError, match=r"out of blocks \(pool size=2\)"):
         m2.append_tokens(s, 0, torch.zeros(12, 1, 64, device="cuda"), torch.zeros(12, 1, 64, device="cuda"))
+
+
+def test_padding_entries_are_skipped():
+    """Slot -1 entries of a batched append (padding of a captured graph's batch)
+    allocate nothing and write nothing: the cache ends as after the same append
+    without them."""
+    from mentat_b200 import PagedKVCacheManager
+
+    def build():
+        m = PagedKVCacheManager(1, 2, 64, max_blocks=32, block_size=4, device="cuda", dtype=torch.float32,
+                                strict=True)
+        a = m.allocate_sequence()
+        base = torch.arange(3 * 2 * 64, dtype=torch.float32, device="cuda").view(3, 2, 64)
+        m.append_tokens(a, 0, base, base)
+        b = m.fork_sequence(a)  # shared partial tail: the append below copies it for one of them
+        return m, a, b
+
+    kv = torch.from_numpy(np.random.default_rng(1).standard_normal((4, 2, 64)).astype(np.float32)).cuda()
+    m1, a, b = build()
+    m1.append_tokens_batched([a, b], 0, kv[[0, 2]], kv[[1, 3]])
+    m2, a2, b2 = build()
+    s = m2._sequences
+    slots = torch.tensor([s[a2].slot, -1, s[b2].slot, -1], dtype=torch.int32, device="cuda")
+    torch.ops.mentat_b200.append_batched(m2._k_all, m2._v_all, slots, kv[[0, 3, 2, 1]], kv[[1, 0, 3, 2]],
+                                         m2._op_id, 0)
+    m2.mirror_decode_step([a2, b2])
+    assert m2.sequence_snapshot() == m1.sequence_snapshot()
+    assert m2.allocator.refcounts == m1.allocator.refcounts
+    assert m2.allocator.free_list() == m1.allocator.free_list()
+    k1, v1, _, _ = m1.packed_kv_tensors([a, b], 0)
+    k2, v2, _, _ = m2.packed_kv_tensors([a2, b2], 0)
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)

@@ -56,6 +56,20 @@ def test_rollout_matches_reference_generator(name):
 
 
 @pytest.mark.parametrize("name", sorted(ROLLOUT_CASES))
+def test_padded_graphs_match_reference_generator(name):
+    """Graphs captured for leaf counts rounded up to a multiple of 4: the padding
+    rows append nothing and attend over an empty sequence, and the trees are the
+    reference's."""
+    c = ROLLOUT_CASES[name]
+    model = rollout_model(c, device="cuda")
+    r = _rollout(c, model, graph_bucket=4)
+    for i, got in enumerate(r.generate_many(rollout_prompts(c))):
+        _check(name, got, GOLDEN[name][i], f"padded prompt {i}")
+    assert all(n % 4 == 0 for n in r.lm._graphs)
+    assert r.cache.get_stats()["blocks_used"] == 0
+
+
+@pytest.mark.parametrize("name", sorted(ROLLOUT_CASES))
 def test_static_decode_matches_reference_generator(name):
     """The eager device-planned step (no graphs) gives the reference's trees too."""
     c = ROLLOUT_CASES[name]
