@@ -313,6 +313,9 @@ def run_tree(args):
                     + "; all trees of a rank advance in lockstep, one forward pass per step; branch threshold = "
                       "90th percentile of a 32-step warm-up's gate entropies",
         }), flush=True)
+    # graphs that hold NCCL calls (tensor parallel) go before the process group does
+    r.lm._graphs = None
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
