@@ -3,8 +3,10 @@
 Each of two ranks builds the same tiny fp32 Qwen3 model, keeps its KV-head shard
 (``tp.shard_model``) and runs ``PagedLM`` over its own cache (two of the four KV
 heads), prefill plus three decode steps with the library's append and decode
-kernels, all-reducing the attention and MLP outputs.  Both ranks must end each
-step with identical logits, equal to the unsplit model's on one GPU.
+kernels, all-reducing the attention and MLP outputs, eagerly and again with the
+decode steps captured as CUDA graphs (all-reduces inside, batch padded).  Both
+ranks must end each step with identical logits, equal to the unsplit model's on
+one GPU.
 Skipped with fewer than two GPUs.
 """
 
@@ -27,13 +29,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(model, device, group):
+def _run(model, device, group, graphs=False):
     from mentat_b200 import PagedKVCacheManager
     from mentat_b200.rollout import PagedLM
     cfg = model.config
     cache = PagedKVCacheManager(cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim, 256, 16, device,
                                 torch.float32, max_seqs=8)
     lm = PagedLM(model, cache, group)
+    if graphs:  # the decode steps as CUDA graphs holding the all-reduces, batch padded to 4
+        lm.enable_graphs(64, 4, bucket=4)
     sid = cache.allocate_sequence()
     out = [lm.prefill(torch.tensor([3, 14, 15, 92, 65, 35, 89, 79, 32, 38, 46, 26, 43, 38, 32, 79, 50, 28],
                                    device=device), sid).float().cpu().numpy()]
@@ -41,6 +45,7 @@ def _run(model, device, group):
         logits, _ = lm.decode(torch.tensor([t], device=device), [sid])
         out.append(logits[0].float().cpu().numpy())
     cache.check()
+    lm._graphs = None  # release graphs holding NCCL calls before the process group goes
     return np.stack(out)
 
 
@@ -62,8 +67,11 @@ def _rank_main(rank, world, port, q):
         with torch.device(device):
             full = Qwen3ForCausalLM(cfg).float().eval()
         want = _run(full, device, None)
-        got = _run(shard_model(full, rank, world), device, dist.group.WORLD)
-        q.put((rank, want, got))
+        shard = shard_model(full, rank, world)
+        got = _run(shard, device, dist.group.WORLD)
+        got_g = _run(shard, device, dist.group.WORLD, graphs=True)
+        torch.cuda.synchronize()
+        q.put((rank, want, got, got_g))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -81,11 +89,13 @@ def test_two_rank_kv_head_split_matches_the_whole_model():
         p.start()
     res = {}
     for _ in range(2):
-        r, want, got = q.get(timeout=240)
-        res[r] = (want, got)
+        r, want, got, got_g = q.get(timeout=240)
+        res[r] = (want, got, got_g)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     np.testing.assert_array_equal(res[0][1], res[1][1])  # identical logits on both ranks
+    np.testing.assert_array_equal(res[0][2], res[1][2])
     for r in range(2):
         np.testing.assert_allclose(res[r][1], res[r][0], atol=1e-4, rtol=1e-4)
+        np.testing.assert_allclose(res[r][2], res[r][1], atol=1e-5, rtol=1e-5)  # graphs = eager
