@@ -27,6 +27,7 @@ from __future__ import annotations
 import ctypes as C
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from . import _lib, ops
@@ -145,19 +146,24 @@ class _PinnedRing:
     def __init__(self, device, depth: int = 16, cap: int = 1024):
         self.device = device
         self.bufs = [torch.empty(cap, dtype=torch.int32, pin_memory=True) for _ in range(depth)]
+        self.views = [b.numpy() for b in self.bufs]
         self.events = [None] * depth
         self.i = 0
 
-    def upload(self, values: torch.Tensor) -> torch.Tensor:
-        n = values.numel()
+    def upload(self, values) -> torch.Tensor:
+        """``values``: int32 numpy array or CPU tensor; returns a device copy."""
+        if isinstance(values, torch.Tensor):
+            values = values.numpy()
+        n = values.size
         k = self.i
         self.i = (k + 1) % len(self.bufs)
         if self.events[k] is not None:
             self.events[k].synchronize()
         if self.bufs[k].numel() < n:
             self.bufs[k] = torch.empty(max(n, 2 * self.bufs[k].numel()), dtype=torch.int32, pin_memory=True)
+            self.views[k] = self.bufs[k].numpy()
+        self.views[k][:n] = values.reshape(-1)
         buf = self.bufs[k][:n]
-        buf.copy_(values)
         dev = torch.empty(n, dtype=torch.int32, device=self.device)
         dev.copy_(buf, non_blocking=True)
         ev = self.events[k] if self.events[k] is not None else torch.cuda.Event()
@@ -287,12 +293,15 @@ class PagedKVCacheManager:
 
     def _slots_dev(self, seq_ids) -> torch.Tensor:
         def make():
-            return self._uploads.upload(torch.tensor([self._sequences[s].slot for s in seq_ids], dtype=torch.int32))
+            seqs = self._sequences
+            return self._uploads.upload(np.fromiter((seqs[s].slot for s in seq_ids), np.int32, len(seq_ids)))
         return self._remember(("slots",) + tuple(seq_ids), make)
 
     def _cu_seqlens(self, lens) -> torch.Tensor:
         def make():
-            return self._uploads.upload(torch.tensor([0] + list(lens), dtype=torch.int32).cumsum(0, dtype=torch.int32))
+            a = np.zeros(len(lens) + 1, np.int32)
+            np.cumsum(lens, out=a[1:])
+            return self._uploads.upload(a)
         return self._remember(("cu",) + tuple(lens), make)
 
     # ------------------------------------------------------------- sequences
@@ -400,11 +409,21 @@ class PagedKVCacheManager:
         N = len(seq_ids)                                    # :227-284
         if N == 0:
             return
-        seqs = [self._sequences[s] for s in seq_ids]
+        seqs = [self._sequences[s] for s in seq_ids]  # an unknown id raises before any change
         k, ks = self._rows(k, N)
         v, vs = self._rows(v, N)
+        # host mirror of one token per sequence, inline (this runs for every layer of
+        # every decode step); the general walk only where a new block would overflow
+        bs, cap, L = self.block_size, self.max_blocks_per_seq, layer_idx
         for s in seqs:
-            self._mirror_append(s, layer_idx, 1)
+            nb, tf = s.num_blocks[L], s.tokens_in_last_block[L]
+            if nb == 0 or tf == bs:
+                if nb + 1 > cap:
+                    self._mirror_append(s, L, 1)  # raises the reference's error
+                s.num_blocks[L], s.tokens_in_last_block[L] = nb + 1, 1
+            else:
+                s.tokens_in_last_block[L] = tf + 1
+            s.num_tokens[L] += 1
         slots = self._slots_dev(seq_ids)
         torch.ops.mentat_b200.append_batched(self._k_all, self._v_all, slots, k, v, self._op_id, layer_idx)
         self._after()
@@ -442,12 +461,25 @@ class PagedKVCacheManager:
 
     # --------------------------------------------------------- decode workspace
     def decode_workspace(self, n: int, hq: int, max_len: int):
+        """The decode workspace for n sequences of up to max_len tokens: (tensor,
+        bytes, partials per sequence).  The partial count is a capacity, so the
+        last answer is reused while it covers the request (lengths grow by one per
+        step), and a new one is sized with headroom."""
+        m = self._ws_memo
+        if m is not None and n <= m[0] and hq == m[1] and max_len <= m[2]:
+            return self._ws, self._ws_bytes, m[3]
+        if m is not None and hq == m[1]:
+            n, max_len = max(n, m[0]), max(max_len, m[2])
+        max_len += 256
         parts = int(self._lib.mentat_decode_max_parts(n, max_len, self.block_size))
         need = int(self._lib.mentat_decode_workspace_bytes(n, hq, self.head_dim, parts))
         if self._ws is None or self._ws_bytes < need:
             self._ws_bytes = max(need, int(self._ws_bytes * 1.5))
             self._ws = torch.empty(self._ws_bytes, device=self.device, dtype=torch.uint8)
+        self._ws_memo = (n, hq, max_len, parts)
         return self._ws, self._ws_bytes, parts
+
+    _ws_memo = None
 
     # ----------------------------------------------------------- sliding window
     def trim_to_window(self, seq_id: int, window_size: int) -> None:   # :370-417
