@@ -1,8 +1,8 @@
-"""Benchmark of the tree-aware paged decode attention.
+"""Benchmark of the tree-aware paged decode attention (benchmark config 4).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mentat|reference]
 
-Workload: bf16, 32 q / 8 kv heads, head_dim 128, KV
+Workload (benchmark config 4): bf16, 32 q / 8 kv heads, head_dim 128, KV
 block 16; one 32768-token shared prefix and 64 branches with suffixes drawn
 from U[1024, 4096] (seeded).  A step is one ``attn_decode`` over the 64
 branches (plan + units + merge kernels).  The unique KV of a step (~0.8 GB) is
@@ -161,19 +161,19 @@ def build_tree(seed, device, extra_blocks):
 
 
 TREE_CONFIGS = {
-    # Qwen3-0.6B architecture, random init, bf16; 4 prompts of 256
+    # benchmark config 2: Qwen3-0.6B architecture, random init, bf16; 4 prompts of 256
     # uniform-random ids, 256 new tokens, at most 8 leaves per tree, KV block 16; one
     # B200 (under torchrun every rank rolls out its own 4 prompts: weak scaling)
     2: dict(family="qwen3", vocab=151936, hidden=1024, intermediate=3072, layers=28, heads=16, kv_heads=8,
             head_dim=128, rope_theta=1000000.0, prompts=4, prompt_len=256, max_new_tokens=256, max_active=8,
             eos=151645, shard=False, graphs=True),
-    # Llama-3.1-8B architecture, random init, bf16; 64 prompts of
+    # benchmark config 3: Llama-3.1-8B architecture, random init, bf16; 64 prompts of
     # 2048 ids, trees of up to 16 leaves, 512 new tokens; the 64 trees are sharded
     # across the ranks (strong scaling)
     3: dict(family="llama", vocab=128256, hidden=4096, intermediate=14336, layers=32, heads=32, kv_heads=8,
             head_dim=128, rope_theta=500000.0, prompts=64, prompt_len=2048, max_new_tokens=512, max_active=16,
             eos=128001, shard=True, graphs=True, bucket=64),
-    # Qwen3-32B architecture, random init, bf16; 32 prompts of 4096
+    # benchmark config 5: Qwen3-32B architecture, random init, bf16; 32 prompts of 4096
     # ids, trees of up to 32 leaves, 1024 new tokens; tensor parallel by KV head over
     # the ranks (one KV head per GPU at 8), NCCL all-reduce after o_proj and down_proj
     5: dict(family="qwen3", vocab=151936, hidden=5120, intermediate=25600, layers=64, heads=64, kv_heads=8,
@@ -393,7 +393,7 @@ def run_profile_kernels(args):
           f"{e0.elapsed_time(e1) / steps * 1e3:.1f} us per pair", flush=True)
     m.check()
     del m
-    # BASELINE config 1 in fp32 (the FFMA unit kernel): Hq 16, Hkv 8, D 128, block 16,
+    # benchmark config 1 in fp32 (the FFMA unit kernel): Hq 16, Hkv 8, D 128, block 16,
     # 8 branches sharing a 512-token prefix, 64 tokens of their own each
     from mentat_b200 import PagedKVCacheManager
     from mentat_b200.attention_backend import attn_decode
@@ -665,7 +665,7 @@ def main():
     ap.add_argument("--profile-kernels", action="store_true",
                     help="time the gate and append kernels for a profiler capture instead of the benchmark")
     ap.add_argument("--tree-config", type=int, default=None, choices=sorted(TREE_CONFIGS),
-                    help="tree tokens/s of the entropy-gated rollout on a BASELINE model config")
+                    help="tree tokens/s of the entropy-gated rollout on a benchmark model config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile_case:

@@ -1,6 +1,6 @@
 """Tensor parallelism by KV head for the rollout's model driver.
 
-The BASELINE's largest model (Qwen3-32B architecture, 8 KV heads) runs split
+The largest benchmark model (Qwen3-32B architecture, 8 KV heads) runs split
 one KV head per GPU: each rank holds its KV heads' query, key and value
 projections (row slices), the matching columns of ``o_proj``, and a slice of
 the MLP's intermediate dimension (rows of ``gate_proj`` / ``up_proj``, columns

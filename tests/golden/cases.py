@@ -68,7 +68,7 @@ def _c(dtype, hq, hkv, d, prefix, levels, seed, pool=1024, bs=16, B=None):
 
 
 ATTN_CASES = {
-    # fp32, 8 branches x (512 shared + 64 own), pool 1024.
+    # benchmark config 1: fp32, 8 branches x (512 shared + 64 own), pool 1024.
     "c1": _c("f32", 16, 8, 128, 512, [(8, (64, 64))], seed=1),
     "f32_ragged": _c("f32", 16, 8, 128, 37, [(3, (0, 40))], seed=2),
     "bf16_b1_g1": _c("bf16", 8, 8, 128, 0, [(1, (1, 1))], seed=3),

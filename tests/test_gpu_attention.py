@@ -54,7 +54,7 @@ def test_decode_matches_reference_golden(name):
 
 
 def c4_like(n_branch, prefix, lo, hi, seed, hq=32, hkv=8, d=128, dtype=torch.bfloat16):
-    """BASELINE config-4 shaped tree built through the cache API."""
+    """Benchmark config-4 shaped tree built through the cache API."""
     from mentat_b200 import PagedKVCacheManager
     g = torch.Generator(device="cuda").manual_seed(seed)
     suf = np.random.default_rng(seed).integers(lo, hi + 1, n_branch)
