@@ -633,16 +633,16 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 // 3. merge: D/64 warps per (sequence, q head), each over 64 output dimensions
 //    (two per lane).  Lane p holds partial p's (m, l); a butterfly of
 //    log-sum-exp combines gives every lane the total (M, L), and lane p's weight
-//    2^(m_p - M) reaches the others by shuffle.  The first 16 partial rows are
-//    all requested before the part count is read; more are taken 16 at a time.
+//    2^(m_p - M) reaches the others by shuffle.  The first 18 partial rows are
+//    all requested before the part count is read; more are taken 18 at a time.
 // ---------------------------------------------------------------------------
 constexpr int MERGE_WARPS = 4;  // warps per CTA
 
 template <typename T, int D>
-__global__ void __launch_bounds__(32 * MERGE_WARPS, 8) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
+__global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
                                                           int max_parts, T* __restrict__ out, int64_t out_stride) {
     constexpr int WPP = D / 64;  // warps per (sequence, head)
-    constexpr int B = 16;        // partial rows in flight per lane (64 registers, no spills)
+    constexpr int B = 18;        // partial rows in flight per lane (config 4 has 17-18 partials)
     griddep_wait();  // every unit kernel's partials
     griddep_launch();
     TL_FIRST(8);
