@@ -209,45 +209,42 @@ def tree_model(c, device, seed):
     return model
 
 
-def run_tree(args):
-    """Tree tokens/s of the entropy-gated rollout (``generator.py:508-511``): decode
-    tokens (one per active leaf per step) over decode wall time, summed over the
-    trees.  The branch threshold is the 90th percentile of the gate entropies of a
-    seeded 32-step warm-up rollout (random-init weights make the adaptive
-    threshold meaningless).  Config 2: every rank rolls out its own prompts (weak
-    scaling); config 3: the prompts are split across the ranks (strong scaling)."""
+def _model_flops_per_token(model) -> float:
+    """2 x the parameters every decoded token multiplies (embedding table excluded)."""
+    n = sum(p.numel() for name, p in model.named_parameters() if "embed_tokens" not in name)
+    return 2.0 * n
+
+
+def tree_measure(cfg_id, seed, rank, world, device):
+    """Tree tokens/s of the entropy-gated rollout on a benchmark model configuration
+    (``generator.py:508-511``): decode tokens (one per active leaf per step) over
+    decode wall time, summed over the trees; the slowest rank's time.  The branch
+    threshold is the 90th percentile of the gate entropies of a seeded 32-step
+    warm-up rollout (random-init weights make the adaptive threshold meaningless).
+    A full warm-up rollout captures the decode graphs before the timed one.  With
+    world > 1 the process group must be up.  Returns a dict (rank 0's view)."""
     import torch.distributed as dist
     from mentat_b200 import _lib
     from mentat_b200.rollout import TreeRollout
-    rank, world, local = _env_rank()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
-    c = TREE_CONFIGS[args.tree_config]
+    c = TREE_CONFIGS[cfg_id]
     tp = bool(c.get("tp"))
     if world < c.get("min_world", 1):
-        if rank == 0:
-            print(json.dumps({"metric": f"tree tokens/s (config {args.tree_config})",
-                              "unavailable": f"needs >= {c['min_world']} GPUs (KV cache of the tree)"}), flush=True)
-        if world > 1:
-            dist.destroy_process_group()
-        return
-    model = tree_model(c, device, args.seed)
+        return {"unavailable": f"needs >= {c['min_world']} GPUs (KV cache of the tree)"}
+    model = tree_model(c, device, seed)
     if tp and world > 1:
         from mentat_b200.tp import shard_model
         full, model = model, shard_model(model, rank, world)
         del full
         torch.cuda.empty_cache()
     if tp:  # every rank rolls out the same trees over its KV heads
-        rng = np.random.default_rng(args.seed * 1000)
+        rng = np.random.default_rng(seed * 1000)
         prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
     elif c["shard"]:
-        rng = np.random.default_rng(args.seed * 1000)
+        rng = np.random.default_rng(seed * 1000)
         allp = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
         prompts = allp[rank::world]
     else:
-        rng = np.random.default_rng(args.seed * 1000 + rank)
+        rng = np.random.default_rng(seed * 1000 + rank)
         prompts = [rng.integers(0, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
     M, K = c["max_active"], 3
     n_trees = len(prompts)
@@ -262,6 +259,7 @@ def run_tree(args):
                     max_blocks_per_seq=-(-(c["prompt_len"] + c["max_new_tokens"]) // 16) + 2,
                     tp_group=dist.group.WORLD if tp and world > 1 else None)
     lib = _lib.load()
+    t_setup = time.perf_counter()
     thr = r.calibrate_threshold(prompts, steps=32, q=90.0)
     if c["graphs"]:
         r.generate_many(prompts)  # warm-up: captures the decode graphs (one per bucket of leaf counts)
@@ -270,7 +268,8 @@ def run_tree(args):
         r.max_new_tokens = 16     # warm-up of the eager path
         r.generate_many(prompts)
         r.max_new_tokens = full
-    r.decode_tokens, r.decode_time_s, r.steps = 0, 0.0, 0
+    warm_s = time.perf_counter() - t_setup
+    r.decode_tokens, r.decode_time_s, r.steps, r.step_leaves = 0, 0.0, 0, []
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -280,42 +279,90 @@ def run_tree(args):
     results = r.generate_many(prompts)
     clk = clocks.stop()
     launches = lib.mentat_kernel_launch_count() + r.lm.graph_kernel_launches - launches0
-    t = torch.tensor([r.decode_time_s], dtype=torch.float64, device=device)
-    tok = torch.tensor([float(r.decode_tokens)], dtype=torch.float64, device=device)
+    # lower bound of this rank's decode time: per step, the weights plus every tree's
+    # prompt KV cross HBM once, and the GEMMs do 2 x params flops per decoded token
+    peak_bw, _ = peaks()
+    peak_fl = _peak_flops()
+    kv_tok = 2 * c["kv_heads"] // (world if tp else 1) * c["head_dim"] * 2 * c["layers"]
+    w_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    fl_tok = _model_flops_per_token(model)
+    bound_s = sum(max((w_bytes + n_trees * c["prompt_len"] * kv_tok) / (peak_bw * 1e9), n * fl_tok / (peak_fl * 1e12))
+                  for n in r.step_leaves)
+    stat = torch.tensor([r.decode_time_s, float(r.decode_tokens), bound_s, float(r.steps)], dtype=torch.float64,
+                        device=device)
+    per_rank = [stat.clone() for _ in range(world)]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        if not tp:  # tensor parallel ranks decode the same tokens
-            dist.all_reduce(tok, op=dist.ReduceOp.SUM)
-    secs, tokens = float(t.item()), float(tok.item())
+        dist.all_gather(per_rank, stat)
+    per_rank = [x.tolist() for x in per_rank]
+    secs = max(x[0] for x in per_rank)
+    tokens = per_rank[0][1] if tp else sum(x[1] for x in per_rank)
     leaves = [len(x) for x in results]
-    if rank == 0:
-        arch = {2: "Qwen3-0.6B", 3: "Llama-3.1-8B", 5: "Qwen3-32B"}[args.tree_config]
-        print(json.dumps({
-            "metric": f"tree tokens/s (config {args.tree_config})", "value": round(tokens / secs, 2),
-            "unit": "tokens/s", "n_gpus": world, "steps": r.steps, "warmup": 1,
-            "ms_per_step": secs / max(r.steps, 1) * 1e3, "higher_is_better": True,
-            "scaling": "strong" if c["shard"] or tp else "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (random-init weights, seeded uniform-random prompt ids)",
-            "config": {"workload": f"BASELINE config {args.tree_config}: {arch} architecture, "
-                                   f"{c['prompts']} prompts x {c['prompt_len']} ids"
-                                   f"{' split across the ranks' if c['shard'] else (' on every rank' if tp else ' per rank')}, "
-                                   f"{c['max_new_tokens']} new tokens, <= {M} leaves per tree",
-                       "decode_tokens": int(tokens), "trees_rank0": n_trees,
-                       "entropy_threshold_rank0": round(thr, 4),
-                       "leaves_per_tree_final_rank0": [min(leaves), float(np.mean(leaves)), max(leaves)],
-                       "parallelism": (f"tensor parallel by KV head x{world} (NCCL all-reduce after o_proj "
-                                       f"and down_proj)" if tp and world > 1 else f"independent trees x{world}")},
-            "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
-            "clocks": clk,
-            "note": (("decode steps run as CUDA graphs" + (f" (leaf counts padded to multiples of {c['bucket']})"
-                                                           if c.get("bucket") else "")) if c["graphs"] else
-                     "eager decode steps planned on the device (no per-layer host work)")
-                    + "; all trees of a rank advance in lockstep, one forward pass per step; branch threshold = "
-                      "90th percentile of a 32-step warm-up's gate entropies",
-        }), flush=True)
+    arch = {2: "Qwen3-0.6B", 3: "Llama-3.1-8B", 5: "Qwen3-32B"}[cfg_id]
+    out = {
+        "metric": f"tree tokens/s (config {cfg_id})", "value": round(tokens / secs, 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": r.steps, "ms_per_step": secs / max(r.steps, 1) * 1e3,
+        "scaling": "strong" if c["shard"] or tp else "weak",
+        "workload": f"BASELINE config {cfg_id}: {arch} architecture, {c['prompts']} prompts x {c['prompt_len']} ids"
+                    f"{' split across the ranks' if c['shard'] else (' on every rank' if tp else ' per rank')}, "
+                    f"{c['max_new_tokens']} new tokens, <= {M} leaves per tree",
+        "decode_tokens": int(tokens), "trees_rank0": n_trees, "entropy_threshold_rank0": round(thr, 4),
+        "leaves_per_tree_final_rank0": [min(leaves), float(np.mean(leaves)), max(leaves)],
+        "per_rank_s": [round(x[0], 3) for x in per_rank], "per_rank_tokens": [int(x[1]) for x in per_rank],
+        "roofline": {"bound_s_rank0": round(per_rank[0][2], 3), "frac_rank0": round(per_rank[0][2] / per_rank[0][0], 4),
+                     "frac_slowest": round(max(x[2] for x in per_rank) / secs, 4),
+                     "what": "per step max(weights + the trees' prompt KV over measured HBM GB/s, "
+                             "2 x params x leaves over measured sustained bf16 TFLOP/s); a lower bound of the "
+                             "decode time (generated-token KV and attention flops not counted)"},
+        "parallelism": (f"tensor parallel by KV head x{world} (NCCL all-reduce after o_proj and down_proj)"
+                        if tp and world > 1 else f"independent trees x{world}"),
+        "gpu_launches": int(launches),  # host launches plus the library kernels inside each graph replayed
+        "clocks": clk, "setup_and_warmup_s": round(warm_s, 1),
+        "note": (("decode steps run as CUDA graphs" + (f" (leaf counts padded to multiples of {c['bucket']})"
+                                                       if c.get("bucket") else "")) if c["graphs"] else
+                 "eager decode steps planned on the device (no per-layer host work)")
+                + "; all trees of a rank advance in lockstep, one forward pass per step; branch threshold = "
+                  "90th percentile of a 32-step warm-up's gate entropies",
+    }
     # graphs that hold NCCL calls (tensor parallel) go before the process group does
     r.lm._graphs = None
+    del r, model
     torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
+def _peak_flops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("bf16_tflops_sustained") or d["bf16_tflops"])
+    return 1400.0
+
+
+def run_tree(args):
+    """``--tree-config N``: tree tokens/s of one benchmark model configuration as
+    its own JSON line (config 2: every rank rolls out its own prompts, weak
+    scaling; config 3: the prompts are split across the ranks, strong scaling;
+    config 5: tensor parallel by KV head)."""
+    import torch.distributed as dist
+    rank, world, local = _env_rank()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
+    out = tree_measure(args.tree_config, args.seed, rank, world, device)
+    if rank == 0:
+        line = {"metric": out.pop("metric", f"tree tokens/s (config {args.tree_config})")}
+        if "unavailable" not in out:
+            line.update({"value": out.pop("value"), "unit": out.pop("unit"), "n_gpus": world,
+                         "steps": out.pop("steps"), "warmup": 1, "ms_per_step": out.pop("ms_per_step"),
+                         "higher_is_better": True, "scaling": out.pop("scaling"), "vs_baseline": None,
+                         "dtype": "bf16", "data": "synthetic (random-init weights, seeded uniform-random prompt ids)",
+                         "config": {"workload": out.pop("workload"), "parallelism": out.pop("parallelism")},
+                         "gpu_launches": out.pop("gpu_launches"), "clocks": out.pop("clocks")})
+        line.update(out)
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -474,39 +521,74 @@ def cpu_sample(m, kids, q, nbranch, budget_s, max_calls=50):
             "seconds_per_call": per}
 
 
+def host_tree(seed):
+    """The config-4 tree built on the host alone (numpy and torch CPU tensors; no
+    GPU and no part of this package): the block tables the device allocator
+    gives ``build_tree`` (a FIFO pool in id order: the 2,048 prefix blocks, then
+    each branch's own blocks in branch order), K/V pools of seeded N(0,1) bf16
+    rows, and q.  Returns (q, k_pool, v_pool, tables, lens, suffixes)."""
+    suf = suffixes(seed)
+    nb_pre = PREFIX // BS
+    own = [(int(n) + BS - 1) // BS for n in suf]
+    total = nb_pre + sum(own)
+    g = torch.Generator().manual_seed(seed)
+    k_pool = torch.randn((total, BS, HKV, D), generator=g).to(torch.bfloat16)
+    v_pool = torch.randn((total, BS, HKV, D), generator=g).to(torch.bfloat16)
+    q = torch.randn((NBR, HQ, D), generator=g).to(torch.bfloat16)
+    tables, nxt = [], nb_pre
+    for n in own:
+        tables.append(list(range(nb_pre)) + list(range(nxt, nxt + n)))
+        nxt += n
+    lens = [PREFIX + int(n) for n in suf]
+    return q, k_pool, v_pool, tables, lens, suf
+
+
+def config4_config(world, ub):
+    return {"workload": "BASELINE config 4: bf16 Hq32/Hkv8/D128, block 16, 32768-token shared prefix "
+                        "+ 64 branches x U[1024,4096]-token suffixes",
+            "unique_kv_bytes_per_step_per_rank": ub, "global_batch": NBR * world,
+            "parallelism": f"independent trees x{world}",
+            "l2": "inputs larger than L2 (unique KV > 126 MB), no flush"}
+
+
 def run_reference(args):
+    """The reference's CPU decode path (``oracle/cpu_path.py``: build_packed_kv +
+    _sdpa_decode with the same torch CPU ops) on the whole config-4 tree, all 64
+    branches per step, on every host thread.  The tree is built on the host, so
+    this arm loads nothing of this package.  If the requested steps would take
+    more than about four minutes, fewer are timed (the line says how many)."""
+    from oracle.cpu_path import decode_step
     rank, world, local = _env_rank()
     if rank != 0:
         return
-    if not torch.cuda.is_available():
-        print(json.dumps({"impl": "reference", "unavailable": "the seeded tree is built on a CUDA device"}))
-        return
-    from oracle.cpu_path import decode_step
-    m, kids, q, suf = build_tree(args.seed, torch.device("cuda", local), 0)
-    torch.cuda.synchronize()
     torch.set_num_threads(os.cpu_count() or 1)
-    cal = cpu_sample(m, kids, q, 1, 0.0)
-    nb = int(max(1, min(8, 150.0 / max(1, args.steps + args.warmup) / max(cal["seconds_per_call"], 1e-3))))
-    qc, kp, vp, tables, lens = _cpu_inputs(m, kids, q, nb)
-    ub = unique_bytes(PREFIX, np.array(lens) - PREFIX)
-    for _ in range(args.warmup):
-        decode_step(qc, kp, vp, tables, lens, BS)
+    q, kp, vp, tables, lens, suf = host_tree(args.seed)
+    ub = unique_bytes(PREFIX, suf)
     t = time.perf_counter()
-    for _ in range(args.steps):
-        decode_step(qc, kp, vp, tables, lens, BS)
-    dt = (time.perf_counter() - t) / args.steps
+    decode_step(q, kp, vp, tables, lens, BS)  # warm-up (one full step)
+    per = time.perf_counter() - t
+    warm = max(0, min(args.warmup, int(60.0 / per)) - 1)
+    for _ in range(warm):
+        decode_step(q, kp, vp, tables, lens, BS)
+    steps = max(1, min(args.steps, int(240.0 / per)))
+    t = time.perf_counter()
+    for _ in range(steps):
+        decode_step(q, kp, vp, tables, lens, BS)
+    dt = (time.perf_counter() - t) / steps
     val = round(ub / dt / 1e9, 4)
-    sample = (f"32768-token prefix + {nb} of 64 branches per step ({ub} unique KV bytes); reference CPU path "
-              "(build_packed_kv + _sdpa_decode) restated in oracle/cpu_path.py")
+    sample = (f"the whole config-4 tree per step: 32768-token prefix + all 64 branches ({sum(lens)} tokens gathered, "
+              f"{ub} unique KV bytes); the reference's CPU path (build_packed_kv + _sdpa_decode) restated in "
+              f"oracle/cpu_path.py; {steps} timed steps after {warm + 1} warm-up")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "steps": steps, "warmup": warm + 1, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, BASELINE config 4 tree)",
-        "config": {"workload": f"config 4 sample: {sample}", "l2": "inputs larger than L2"},
+        "config": config4_config(1, ub),
         "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "steps_requested": args.steps, "warmup_requested": args.warmup,
     }), flush=True)
 
 
@@ -518,7 +600,7 @@ def run_mentat(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
     lib = _lib.load()
     m, kids, q, suf = build_tree(args.seed + rank, device,
                                  extra_blocks=NBR * ((args.steps + args.warmup) // BS + 2))
@@ -625,16 +707,24 @@ def run_mentat(args):
         if world == 1 and not args.no_cpu:
             cpu = cpu_sample(m, kids, q, 2, 12.0)
             cpu.pop("seconds_per_call", None)
+    h2d_bytes, d2h_bytes = int(in_host[0].numel() * 2), int(out_host.numel() * 2)
+    # tree tokens/s of benchmark config 3 on the same ranks (the prompts split across them)
+    del m, k, v, cu, q, in_host
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    tree = None
+    if args.tree:
+        try:
+            tree = tree_measure(3, args.seed, rank, world, device)
+        except Exception as e:  # noqa: BLE001 - the headline line is printed either way
+            tree = {"metric": "tree tokens/s (config 3)", "error": f"{type(e).__name__}: {e}"[:300]}
+    if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v, BASELINE config 4 tree per rank)",
-            "config": {"workload": "BASELINE config 4: bf16 Hq32/Hkv8/D128, block 16, 32768-token shared prefix "
-                                   "+ 64 branches x U[1024,4096]-token suffixes",
-                       "unique_kv_bytes_per_step_per_rank": ub, "global_batch": NBR * world,
-                       "parallelism": f"independent trees x{world}",
-                       "l2": "inputs larger than L2 (unique KV > 126 MB), no flush"},
+            "config": config4_config(world, ub),
             "roofline": {"bound": "hbm",
                          "kernel": {"units_tc": "k_units_tc", "units_tcn": "k_units_tcn", "units_ffma": "k_units"}[dom],
                          "achieved": round(achieved, 2) if achieved else None, "peak": peak, "unit": "GB/s",
@@ -645,12 +735,13 @@ def run_mentat(args):
                                         "GBps": round(ub / (ms_max / args.steps / 1e3) / 1e9, 1)}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": int(in_host[0].numel() * 2),
-                    "d2h_bytes_per_step": int(out_host.numel() * 2),
+                    "h2d_bytes_per_step": h2d_bytes,
+                    "d2h_bytes_per_step": d2h_bytes,
                     "path": "pinned H2D of [q | new K | new V] in one copy -> append_tokens_batched -> "
                             "build_packed_kv -> attn_decode -> D2H output"},
             "gpu_launches": int(launches),  # counted by the library over the device-timed loop
             "clocks": clk,
+            "tree": tree,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -666,6 +757,8 @@ def main():
     ap.add_argument("--impl", default="mentat", choices=["mentat", "reference"])
     ap.add_argument("--seed", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-tree", dest="tree", action="store_false",
+                    help="skip the config-3 tree tokens/s measurement of the default run")
     ap.add_argument("--profile-case", default=None, metavar="PREFIX,BRANCHES,SUFFIX",
                     help="time a smaller tree for a profiler capture instead of the benchmark")
     ap.add_argument("--profile-kernels", action="store_true",

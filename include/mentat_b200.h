@@ -36,6 +36,9 @@ extern "C" {
 #define MENTAT_DEV_PLAN_OVERFLOW 4   /* decode plan exceeded its workspace */
 #define MENTAT_DEV_TABLE_OVERFLOW 5  /* a sequence outgrew max_blocks_per_seq */
 #define MENTAT_DEV_DECODE_TIMEOUT 6  /* a bounded wait in a decode kernel gave up; that call's output is invalid */
+#define MENTAT_DEV_BAD_BLOCK 7       /* a block table entry outside [0, num_blocks) (ctrl[ERRARG] = the entry),
+                                        which the decode and gather kernels do not read; that call's output is
+                                        invalid.  The reference asserts on bad block ids at paged_kv_cache.py:59,63 */
 
 /* dtypes */
 #define MENTAT_F32 0
@@ -168,6 +171,15 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
 int mentat_paged_decode_noalloc(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
                                 const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
                                 int64_t out_stride, float scale, int32_t max_parts, cudaStream_t s);
+
+/* Test hook for the bounded waits of the tensor-core decode kernels.  No
+ * counterpart in the reference.  With cycles > 0, every CTA of those kernels
+ * first waits, for at most `cycles` clock cycles, on a barrier that nothing
+ * arrives on; the wait gives up before the CTA has issued any copy or MMA, the
+ * CTA takes its timeout path, and the call reports MENTAT_DEV_DECODE_TIMEOUT
+ * in the cache's control words with its output zeroed.  0 (the default) turns
+ * the hook off.  Applies to the current device, synchronously. */
+int mentat_decode_set_wait_probe(int64_t cycles);
 
 /* Stage timing of mentat_paged_decode with CUDA events recorded on the launch
  * stream, for up to max_records launches (0 disables).  No counterpart in the

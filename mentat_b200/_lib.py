@@ -18,7 +18,7 @@ MENTAT_F32, MENTAT_BF16, MENTAT_F16 = 0, 1, 2
 CTRL_HEAD, CTRL_TAIL, CTRL_PEAK, CTRL_ERROR, CTRL_ERRARG, CTRL_ALLOCS, CTRL_COWS = range(7)
 CTRL_WORDS = 16
 DEV_OUT_OF_BLOCKS, DEV_REF_FREE, DEV_RELEASE_FREE, DEV_PLAN_OVERFLOW, DEV_TABLE_OVERFLOW = 1, 2, 3, 4, 5
-DEV_DECODE_TIMEOUT = 6
+DEV_DECODE_TIMEOUT, DEV_BAD_BLOCK = 6, 7
 GATE_MAXK = 8
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 ERR_SCRATCH_LIMIT = -4
@@ -72,6 +72,7 @@ SIGNATURES = [
     ("mentat_decode_max_parts", _I32, [_I32, _I32, _I32]),
     ("mentat_paged_decode", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
     ("mentat_paged_decode_noalloc", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _I32, _P]),
+    ("mentat_decode_set_wait_probe", C.c_int, [_I64]),
     ("mentat_profile_enable", C.c_int, [_I32]),
     ("mentat_profile_collect", C.c_int, [C.POINTER(C.c_double), C.POINTER(_I32)]),
     ("mentat_kernel_launch_count", C.c_int64, []),

@@ -31,6 +31,10 @@ __device__ long long g_plan_trace[16];
 
 namespace mentat {
 
+// cycles of the test hook's wait in every tensor-core unit CTA (0: off); set by
+// mentat_decode_set_wait_probe
+__device__ long long g_decode_wait_probe = 0;
+
 constexpr int PLAN_HDR = 64;        // header ints, see HDR_*
 constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC_NEXT = 4, HDR_TC_ABORT = 5,
               HDR_NTCN = 6, HDR_TCN_NEXT = 7;
@@ -538,9 +542,15 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
                     const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
                     if (j < cnt) {
                         const int p = t0 + j;
-                        const int64_t off = pool_row(c, layer, tab[p / bs], p % bs) + (int64_t)head * D + d;
-                        kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
-                        vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
+                        const int blk = tab[p / bs];
+                        if ((unsigned)blk < (unsigned)c.num_blocks) {
+                            const int64_t off = pool_row(c, layer, blk, p % bs) + (int64_t)head * D + d;
+                            kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
+                            vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
+                        } else {  // a corrupt table entry: recorded, and read as zeros
+                            set_error(c, MENTAT_DEV_BAD_BLOCK, blk);
+                            kr[k] = vr[k] = make_uint4(0, 0, 0, 0);
+                        }
                     }
                 }
 #pragma unroll
@@ -661,10 +671,13 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
 #pragma unroll
     for (int j = 0; j < B; ++j)
         if (j < max_parts) v[j] = po[j * ostride];
-    const int P = ws.nparts[i];
-    // a tensor-core unit kernel that gave up a bounded wait left partials unwritten
-    const bool aborted = ws.hdr[HDR_TC_ABORT] != 0;
-    if (aborted && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
+    // A failed plan (HDR_ERR) stored part counts that may exceed max_parts and
+    // wrote no units; a tensor-core unit kernel that gave up a bounded wait left
+    // partials unwritten.  Either way the output is zeroed, and the part count
+    // is clamped so that no row past the workspace is read.
+    const bool aborted = ws.hdr[HDR_TC_ABORT] != 0 || ws.hdr[HDR_ERR] != 0;
+    const int P = aborted ? 0 : min(ws.nparts[i], max_parts);
+    if (ws.hdr[HDR_TC_ABORT] != 0 && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
     // (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
     auto comb = [](float& m, float& l, float m2, float l2) {
         const float mn = fmaxf(m, m2);
@@ -786,8 +799,11 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
             tc_ok = maps != nullptr;
         }
         narrow_ok = tc_ok && D == 128 && narrow_enabled();
-        static bool attr = false;
-        if (tc_ok && !attr) {
+        // the shared-memory attribute is per device: one flag per device ordinal
+        static bool attr[64] = {};
+        int dev = 0;
+        if (tc_ok && (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)) return MENTAT_ERR_CUDA;
+        if (tc_ok && !attr[dev]) {
             if (cudaFuncSetAttribute(k_units_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
                 cudaSuccess)
                 return MENTAT_ERR_CUDA;
@@ -795,7 +811,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
                 if (cudaFuncSetAttribute(k_units_tcn<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, TCN_SMEM) !=
                     cudaSuccess)
                     return MENTAT_ERR_CUDA;
-            attr = true;
+            attr[dev] = true;
         }
     }
     PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows()};
@@ -890,6 +906,16 @@ int mentat_profile_collect(double* stage_ms, int32_t* launches) {
             stage_ms[st] += ms;
         }
     g_prof_n = 0;
+    return MENTAT_OK;
+}
+
+int mentat_decode_set_wait_probe(int64_t cycles) {
+    if (cycles < 0) return MENTAT_ERR_ARG;
+    const long long v = cycles;
+    if (cudaMemcpyToSymbol(g_decode_wait_probe, &v, sizeof(v)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return MENTAT_ERR_CUDA;
+    }
     return MENTAT_OK;
 }
 

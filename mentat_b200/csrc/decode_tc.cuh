@@ -83,13 +83,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// bounded wait: false on timeout
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// bounded wait: false once `limit` clock cycles have passed
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, long long limit) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > TC_WAIT_CYCLES) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, TC_WAIT_CYCLES);
+}
+// Test hook (mentat_decode_set_wait_probe): when g_decode_wait_probe > 0, one
+// thread of every tensor-core unit CTA first waits on `probe_bar`, which nothing
+// arrives on, for that many cycles.  The wait gives up, and the CTA takes its
+// ordinary timeout path before it has issued any copy or MMA.
+__device__ __forceinline__ bool wait_probe(uint32_t probe_bar) {
+    const long long limit = g_decode_wait_probe;
+    return limit <= 0 || mbar_wait_for(probe_bar, 0, limit);
+}
+// A table entry outside [0, num_blocks) is recorded as MENTAT_DEV_BAD_BLOCK and
+// replaced by the row just past the pool, which TMA reads as zeros.
+__device__ __forceinline__ int checked_block(const mentat_kv_cache& c, int b) {
+    if ((unsigned)b < (unsigned)c.num_blocks) return b;
+    set_error(c, MENTAT_DEV_BAD_BLOCK, b);
+    return c.num_blocks;
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
     asm volatile(
@@ -339,6 +357,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     __shared__ uint32_t s_tmem;
     __shared__ int s_work, s_abort;
     __shared__ int s_blk[MAX_BLK];
+    __shared__ __align__(8) uint64_t s_probe_bar;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool issuer = (warp >= TC_SOFTMAX_WARPS);
     const bool leader = warp == TC_SOFTMAX_WARPS && lane == 0;  // MMA issue
@@ -370,6 +389,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
             mbar_init(bar_p0 + 8 * rt, 4);  // one arrival per softmax warp of the row tile
             mbar_init(bar_o0 + 8 * rt, 1);
         }
+        mbar_init(smem_u32(&s_probe_bar), 1);
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -384,6 +404,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     // narrow kernel after this one may start on the SMs this one leaves free.
     griddep_wait();
     griddep_launch();
+    if (tid == 0 && !wait_probe(smem_u32(&s_probe_bar))) s_abort = 1;  // seen after the loop's first barrier
     TL_FIRST(4);
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
@@ -417,7 +438,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
             constexpr int PER_LANE = (MAX_BLK + 31) / 32;
             int b[PER_LANE];
 #pragma unroll
-            for (int k = 0; k < PER_LANE; ++k) b[k] = lane + 32 * k < nblk ? tab[blk0 + lane + 32 * k] : 0;
+            for (int k = 0; k < PER_LANE; ++k) b[k] = lane + 32 * k < nblk ? checked_block(c, tab[blk0 + lane + 32 * k]) : 0;
 #pragma unroll
             for (int k = 0; k < PER_LANE; ++k)
                 if (lane + 32 * k < nblk) s_blk[lane + 32 * k] = b[k];

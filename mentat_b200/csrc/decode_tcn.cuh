@@ -91,6 +91,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tcn_smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
+    __shared__ __align__(8) uint64_t s_probe_bar;
     __shared__ int s_unit[2][8];  // per unit slot: q_lo, q_hi, t0u, t1u, ord, head, valid, sequence slot
     __shared__ float s_mref[TCN_ROWS], s_fac[TCN_ROWS], s_red[4][TCN_ROWS];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -117,6 +118,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
             mbar_init(bar_ufull0 + 8 * b, 1);
             mbar_init(bar_uempty0 + 8 * b, 1);
         }
+        mbar_init(smem_u32(&s_probe_bar), 1);
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -132,6 +134,8 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     // the wide one until its end, so the two overlap on the SMs the wide kernel
     // leaves free.
     griddep_launch();
+    if (tid == 0 && !wait_probe(smem_u32(&s_probe_bar))) s_abort = 1;
+    __syncthreads();  // every role sees the probe's outcome before it claims or streams a unit
     TL_FIRST(6);
 
 #ifdef MENTAT_TC_TRACE
@@ -204,11 +208,12 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
             const int32_t* tab = table_row(c, layer, s_unit[slot][7]);
             const int blk0 = t0u / 16, nblk = (t1u + 15) / 16 - blk0;
             const int ntiles = (nblk + 7) / 8;
-            int next = (lane < 8 && lane < nblk) ? tab[blk0 + lane] : 0;
+            int next = (lane < 8 && lane < nblk) ? checked_block(c, tab[blk0 + lane]) : 0;
             for (int i = 0; i < ntiles; ++i) {
                 const int blk = next;
                 const int nb = min(8, nblk - 8 * i);
-                if (i + 1 < ntiles) next = (lane < 8 && 8 * (i + 1) + lane < nblk) ? tab[blk0 + 8 * (i + 1) + lane] : 0;
+                if (i + 1 < ntiles)
+                    next = (lane < 8 && 8 * (i + 1) + lane < nblk) ? checked_block(c, tab[blk0 + 8 * (i + 1) + lane]) : 0;
                 const uint32_t gi = issued, stage = gi % TCN_NST;
                 const uint32_t bar = bar_full0 + 8 * stage;
                 if (lane == 0) {

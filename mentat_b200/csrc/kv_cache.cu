@@ -528,6 +528,10 @@ __global__ void k_gather(mentat_kv_cache c, int layer, const int32_t* slots, int
         }
         const int t = (int)(p - cu[lo]);
         const int b = table_row(c, layer, slots[lo])[t / c.block_size];
+        if ((unsigned)b >= (unsigned)c.num_blocks) {  // a corrupt table entry: recorded, the row left as is
+            if (threadIdx.x == 0) set_error(c, MENTAT_DEV_BAD_BLOCK, b);
+            continue;
+        }
         const int64_t off = pool_row(c, layer, b, t % c.block_size) * esz;
         block_copy_bytes(ok + p * row_bytes, reinterpret_cast<uint8_t*>(c.k_pool) + off, row_bytes);
         block_copy_bytes(ov + p * row_bytes, reinterpret_cast<uint8_t*>(c.v_pool) + off, row_bytes);
@@ -563,6 +567,8 @@ const char* mentat_status_string(int s) {
         case MENTAT_DEV_RELEASE_FREE: return "release() on free block";
         case MENTAT_DEV_PLAN_OVERFLOW: return "decode plan workspace overflow";
         case MENTAT_DEV_TABLE_OVERFLOW: return "sequence table overflow";
+        case MENTAT_DEV_DECODE_TIMEOUT: return "a bounded wait in a decode kernel gave up";
+        case MENTAT_DEV_BAD_BLOCK: return "block table entry outside the pool";
         default: return "unknown status";
     }
 }

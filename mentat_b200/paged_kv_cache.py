@@ -274,10 +274,16 @@ class PagedKVCacheManager:
                                f"max_blocks_per_seq={self.max_blocks_per_seq})")
         if err == _lib.DEV_PLAN_OVERFLOW:
             raise RuntimeError("mentat_b200: decode plan workspace overflow")
+        if err == _lib.DEV_BAD_BLOCK:
+            raise AssertionError(f"block table entry {arg} outside the pool (max_blocks={self.max_blocks})")
         if err == _lib.DEV_DECODE_TIMEOUT:
             raise RuntimeError(f"mentat_b200: a decode kernel's bounded wait gave up (stage {arg}); "
                                "that call's output is invalid")
         raise RuntimeError(f"mentat_b200 device error {err} ({arg})")
+
+    def clear_error(self) -> None:
+        """Forget the recorded device error (after the caller has handled it)."""
+        self._ctrl[_lib.CTRL_ERROR:_lib.CTRL_ERRARG + 1].zero_()
 
     def _after(self):
         if self.strict:
@@ -474,12 +480,24 @@ class PagedKVCacheManager:
         parts = int(self._lib.mentat_decode_max_parts(n, max_len, self.block_size))
         need = int(self._lib.mentat_decode_workspace_bytes(n, hq, self.head_dim, parts))
         if self._ws is None or self._ws_bytes < need:
+            if self._ws is not None and self._ws_pinned:
+                # captured CUDA graphs hold the old address: it must stay allocated
+                self._ws_retired.append(self._ws)
             self._ws_bytes = max(need, int(self._ws_bytes * 1.5))
             self._ws = torch.empty(self._ws_bytes, device=self.device, dtype=torch.uint8)
         self._ws_memo = (n, hq, max_len, parts)
         return self._ws, self._ws_bytes, parts
 
     _ws_memo = None
+    _ws_pinned = False
+
+    def pin_workspace(self) -> None:
+        """From now on a workspace that is outgrown stays allocated (for the
+        lifetime of the cache), because CUDA graphs captured over it keep
+        writing to its address on every replay."""
+        if not self._ws_pinned:
+            self._ws_pinned = True
+            self._ws_retired = []
 
     # ----------------------------------------------------------- sliding window
     def trim_to_window(self, seq_id: int, window_size: int) -> None:   # :370-417

@@ -246,6 +246,7 @@ class PagedLM:
             if self._pad_seq is None:
                 self._pad_seq = self.cache.allocate_sequence()  # never appended to: length 0
         self.cache.decode_workspace(max_n, self.hq, max_len)
+        self.cache.pin_workspace()
         self._graph_max_len = max_len
         self._graph_max_n = max_n
         self._graphs = {}
@@ -310,12 +311,16 @@ class PagedLM:
     def decode(self, tokens: torch.Tensor, seq_ids: list) -> tuple:
         """One token per sequence: logits (N, V) and final hidden states (N, D)."""
         N = len(seq_ids)
-        if self._graphs is not None and N <= self._graph_max_n:
+        seq = self.cache._sequences
+        # captured and static steps size their workspace for _graph_max_len tokens
+        # (the new one included); longer sequences take the eager path
+        fits = (self._graphs is not None or self._static_max_len is not None) and \
+            max(seq[s].num_tokens[0] for s in seq_ids) < self._graph_max_len
+        if fits and self._graphs is not None and N <= self._graph_max_n:
             if self._bucket:
                 Nb = -(-N // self._bucket) * self._bucket
                 g = self._graphs.get(Nb) or self._capture(Nb)
                 # the padding rows: token 0, no append (slot -1), attention over the empty sequence
-                seq = self.cache._sequences
                 pad = seq[self._pad_seq].slot
                 sl = [seq[s].slot for s in seq_ids]
                 both = torch.tensor([sl + [-1] * (Nb - N), sl + [pad] * (Nb - N)], dtype=torch.int32)
@@ -332,7 +337,7 @@ class PagedLM:
             self.graph_kernel_launches += g["kernels"]
             self.cache.mirror_decode_step(seq_ids)
             return g["logits"][:N], g["hidden"][:N]
-        if self._static_max_len is not None:
+        if fits and self._static_max_len is not None:
             out = self._forward_static(tokens.view(N), self.cache._slots_dev(seq_ids))
             self.cache.mirror_decode_step(seq_ids)
             return out
@@ -462,6 +467,7 @@ class TreeRollout:
         self.decode_tokens = 0       # one per active leaf per decode step (step 0 excluded)
         self.decode_time_s = 0.0
         self.steps = 0
+        self.step_leaves = []        # sequences decoded at each step
 
     # ---- per-leaf decision (generator.py:250-374) ---------------------------
     def _records(self, recs) -> list:
@@ -574,6 +580,7 @@ class TreeRollout:
             if not leaves:
                 break
             self.steps += 1
+            self.step_leaves.append(len(leaves))
             tokens = torch.tensor([lf.token_ids[-1] for lf in leaves], dtype=torch.long).to(self.device,
                                                                                               non_blocking=True)
             logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])
@@ -623,7 +630,7 @@ class TreeRollout:
         entropies of a ``steps``-step rollout of ``prompts`` without branching;
         returns it.  The counters of that rollout are discarded."""
         keep = (self.max_new_tokens, self.decode_tokens, self.decode_time_s, self.steps, self.cuda_graphs,
-                self.static_decode)
+                self.static_decode, list(self.step_leaves))
         self.entropy_threshold, self.entropy_log = math.inf, []
         # host-planned steps: graphs or the static path set up now would size their
         # workspace for this short rollout
@@ -633,7 +640,7 @@ class TreeRollout:
             log = self.entropy_log[len(prompts):]  # the decode steps (step 0 is the prompt's own)
         finally:
             (self.max_new_tokens, self.decode_tokens, self.decode_time_s, self.steps, self.cuda_graphs,
-             self.static_decode) = keep
+             self.static_decode, self.step_leaves) = keep
             self.entropy_log = None
         self.entropy_threshold = float(np.percentile(np.asarray(log, np.float64), q))
         return self.entropy_threshold

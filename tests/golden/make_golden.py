@@ -32,7 +32,9 @@ import torch.nn.functional as F
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
-REF = os.environ.get("MENTAT_REF", "/root/reference")
+REF = os.environ.get("MENTAT_REF")
+if not REF:
+    sys.exit("set MENTAT_REF to the reference checkout (the directory holding core/ and adapters/)")
 sys.path.insert(0, REF)
 
 import adapters.attention_backend as ab  # noqa: E402

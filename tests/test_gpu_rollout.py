@@ -113,3 +113,43 @@ def test_calibrated_threshold_is_the_warmup_percentile():
     thr = r.calibrate_threshold(prompts, steps=8, q=75.0)
     assert thr == want
     assert r.entropy_threshold == thr and r.max_new_tokens == keep and r.decode_tokens == 8 * len(prompts)
+
+
+def test_graph_workspace_outlives_eager_growth():
+    """Captured decode graphs keep writing to the workspace address they were
+    captured with.  An eager step that needs a larger workspace must not hand
+    the old one back to the allocator: a tensor allocated afterwards must not
+    be overwritten by the next replay, and the replayed step must still equal
+    the same step run eagerly."""
+    from mentat_b200 import PagedKVCacheManager
+    from mentat_b200.rollout import PagedLM
+    c = ROLLOUT_CASES["qwen3_fp32"]
+    model = rollout_model(c, device="cuda")
+    prompt = torch.tensor(rollout_prompts(c)[0], device="cuda")
+
+    def setup():
+        cache = PagedKVCacheManager(c["layers"], c["kv_heads"], c["head_dim"], max_blocks=512, block_size=16,
+                                    device="cuda", dtype=torch.float32)
+        lm = PagedLM(model, cache)
+        root = cache.allocate_sequence()
+        lm.prefill(prompt, root)
+        kids = [cache.fork_sequence(root) for _ in range(3)]
+        return cache, lm, kids
+
+    tok = lambda n, s: torch.arange(5 + s, 5 + s + n, device="cuda")  # noqa: E731
+    cache, lm, kids = setup()
+    lm.enable_graphs(max_len=64, max_n=2)
+    lm.decode(tok(2, 0), kids[:2])                       # captured (N = 2)
+    old = cache._ws.data_ptr()
+    lm.decode(tok(3, 1), kids)                           # eager (N = 3 > max_n): a larger workspace
+    assert cache._ws.data_ptr() != old
+    junk = [torch.full((cache._ws_retired[0].numel(),), 7, dtype=torch.uint8, device="cuda") for _ in range(4)]
+    got, _ = lm.decode(tok(2, 2), kids[:2])              # replay of the N = 2 graph
+    torch.cuda.synchronize()
+    assert all(bool((j == 7).all()) for j in junk)
+    cache.check()
+    ref_cache, ref_lm, ref_kids = setup()                # the same three steps, eagerly
+    ref_lm.decode(tok(2, 0), ref_kids[:2])
+    ref_lm.decode(tok(3, 1), ref_kids)
+    want, _ = ref_lm.decode(tok(2, 2), ref_kids[:2])
+    torch.testing.assert_close(got, want, atol=1e-5, rtol=1e-5)
