@@ -134,7 +134,7 @@ int mentat_kv_gather(const mentat_kv_cache* c, int32_t layer, const int32_t* slo
  * (paged_kv_cache.py:289-368, attention_backend.py:192-228 -> flash_attn varlen
  * or _sdpa_decode :99-168).  Sequences are the slots of the batch, in batch
  * order; KV blocks shared by adjacent sequences of the batch (found from the
- * block tables) are read once for all of them.  n <= 512 per call.
+ * block tables) are read once for all of them.  n <= 1024 per call.
  *
  * q:   [n][num_q_heads][head_dim], token stride q_stride (elements), cache dtype.
  * out: same layout, out_stride.
@@ -148,6 +148,22 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
                         const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
                         int64_t out_stride, float scale, void* workspace, int64_t workspace_bytes,
                         int32_t max_parts, cudaStream_t s);
+
+/* The same decode for another layer of the same step, with the plan that an
+ * earlier mentat_paged_decode call left in the workspace.  Replaces the per-layer
+ * build_packed_kv + attn_decode of decode_batch (generator_utils.py:381-410) for
+ * every layer after the first: forks copy all layers' tables and a decode step
+ * appends to every layer, so all layers share one sharing structure, and the
+ * partition of the batch into shared segments and units found for one layer
+ * holds for the others.  The workspace must hold the plan of a call on the same
+ * stream with the same slots, n, num_q_heads and max_parts, made after the
+ * sequences last changed in every layer.  A workspace planned for another n,
+ * max_parts, GQA group or routing runs no unit, zeroes the output and records
+ * MENTAT_DEV_PLAN_OVERFLOW. */
+int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, const int32_t* slots,
+                                   int32_t n, const void* q, int64_t q_stride, int32_t num_q_heads,
+                                   void* out, int64_t out_stride, float scale, void* workspace,
+                                   int64_t workspace_bytes, int32_t max_parts, cudaStream_t s);
 
 /* Decode for callers that cannot allocate device memory when they call.
  * No counterpart in the reference.  Some hosts cannot hand this library a
@@ -215,8 +231,16 @@ typedef struct mentat_gate_params {
     int32_t num_active;     /* active leaves at the start of the step */
     int32_t step;           /* decode step */
     int32_t window;         /* soft_explore_window */
-    int32_t pad;
+    int32_t flags;          /* MENTAT_GATE_* bits, 0 by default */
 } mentat_gate_params;
+/* flags: leave pen_entropy out (0 in the record).  The reference computes it only
+ * for its branch-point diagnostics (generator.py:291-293), not for a decision. */
+#define MENTAT_GATE_SKIP_PEN_ENTROPY 1
+/* flags: log-softmax as (x - max) - log(S) with log(S) in float and one rounding,
+ * which is how torch's CUDA kernels compute it; the default rounds log(S) to the
+ * logits dtype first, as torch's CPU kernels do (the rounding chain the golden
+ * fixtures pin).  Both are the reference's own arithmetic on its two devices. */
+#define MENTAT_GATE_FLOAT_LOGSUM 2
 
 typedef struct mentat_gate_out {
     double entropy;         /* compute_entropy(logits, T), reduced-precision rounding chain */

@@ -20,6 +20,7 @@ CTRL_WORDS = 16
 DEV_OUT_OF_BLOCKS, DEV_REF_FREE, DEV_RELEASE_FREE, DEV_PLAN_OVERFLOW, DEV_TABLE_OVERFLOW = 1, 2, 3, 4, 5
 DEV_DECODE_TIMEOUT, DEV_BAD_BLOCK = 6, 7
 GATE_MAXK = 8
+GATE_SKIP_PEN_ENTROPY, GATE_FLOAT_LOGSUM = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 ERR_SCRATCH_LIMIT = -4
 
@@ -40,7 +41,7 @@ class GateParams(C.Structure):
     _fields_ = [
         ("temperature", C.c_double), ("penalty", C.c_double), ("alpha", C.c_double),
         ("mult", C.c_double), ("initial", C.c_double), ("K", C.c_int32), ("M", C.c_int32),
-        ("num_active", C.c_int32), ("step", C.c_int32), ("window", C.c_int32), ("pad", C.c_int32),
+        ("num_active", C.c_int32), ("step", C.c_int32), ("window", C.c_int32), ("flags", C.c_int32),
     ]
 
 
@@ -71,6 +72,8 @@ SIGNATURES = [
     ("mentat_decode_workspace_bytes", _I64, [_I32, _I32, _I32, _I32]),
     ("mentat_decode_max_parts", _I32, [_I32, _I32, _I32]),
     ("mentat_paged_decode", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
+    ("mentat_paged_decode_reuse_plan", C.c_int,
+     [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
     ("mentat_paged_decode_noalloc", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _I32, _P]),
     ("mentat_decode_set_wait_probe", C.c_int, [_I64]),
     ("mentat_profile_enable", C.c_int, [_I32]),

@@ -51,7 +51,7 @@ def attn_decode(q: torch.Tensor, k, v, cu_seqlens_q: torch.Tensor = None, cu_seq
     if n == 0:
         return torch.empty((0, hq, d), device=q.device, dtype=q.dtype)
     scale = 1.0 / math.sqrt(d) if softmax_scale is None else float(softmax_scale)
-    out = torch.ops.mentat_b200.paged_decode(q[:n], k.slots, max(k.lens), mgr._op_id, k.layer, scale)
+    out = ops.paged_decode(q[:n], k.slots, max(k.lens), mgr._op_id, k.layer, scale)
     if mgr.strict:
         mgr.check()
     return out

@@ -38,6 +38,10 @@ __device__ long long g_decode_wait_probe = 0;
 constexpr int PLAN_HDR = 64;        // header ints, see HDR_*
 constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC_NEXT = 4, HDR_TC_ABORT = 5,
               HDR_NTCN = 6, HDR_TCN_NEXT = 7;
+// what the plan was made for, checked by a call that reuses it: n, max_parts,
+// the GQA group, and the routing (tensor-core kernels on, narrow kernel on,
+// row threshold)
+constexpr int HDR_PLAN_N = 8, HDR_PLAN_PARTS = 9, HDR_PLAN_G = 10, HDR_PLAN_ROUTE = 11;
 constexpr int KIND_FFMA = 0, KIND_TC = 1, KIND_TCN = 2, NKINDS = 3;
 constexpr int UNIT_INTS = 8;        // seq_lo, seq_hi, tok0, tok1, ordinal
 constexpr int CHUNK = 256;          // tokens per FFMA unit
@@ -45,7 +49,9 @@ constexpr int CHUNK_TC = 2048;      // tokens per tensor-core unit
 constexpr int MAX_ROWS = 16;        // query rows per unit on the FFMA path
 constexpr int TC_MAX_ROWS = 256;    // query rows per unit on the wide tensor-core path (two M=128 tiles)
 constexpr int TCN_MAX_ROWS = 32;    // query rows per unit on the narrow (transposed) tensor-core path
-constexpr int PLAN_MAX_SEQS = 512;  // sequences per launch (callers split larger batches)
+constexpr int PLAN_MAX_SEQS = 1024;  // sequences per launch (callers split larger batches)
+// the plan's shared memory (dynamic, sized by n): 22 n + 2 ints, see k_plan
+__host__ __device__ inline int plan_smem_bytes(int n) { return (22 * n + 2) * 4; }
 
 struct DecodeWs {
     int32_t* hdr;
@@ -156,6 +162,10 @@ struct PlanParams {
 
 constexpr int LPT_BUCKETS = CHUNK_TC / 128;  // tensor-core units by 128-token tile count
 
+__host__ __device__ inline int plan_route(const PlanParams& pp) {
+    return pp.tc_ok | (pp.narrow_ok << 1) | (pp.tc_min_rows << 2);
+}
+
 __device__ __forceinline__ int seg_kind(const PlanParams& pp, int width) {
     const int rows = width * pp.G;
     if (!pp.tc_ok || rows < pp.tc_min_rows) return KIND_FFMA;
@@ -170,16 +180,25 @@ __device__ __forceinline__ int seg_spu(const PlanParams& pp, int kind) {
 
 __global__ void __launch_bounds__(1024)
 k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp, DecodeWs ws, int max_parts) {
-    __shared__ int s_len[PLAN_MAX_SEQS];
-    __shared__ int s_slot[PLAN_MAX_SEQS];
-    __shared__ int s_h[PLAN_MAX_SEQS + 1];    // h[i] = LCP(i-1, i) in tokens, h[0] = h[n] = 0
-    __shared__ int s_top[PLAN_MAX_SEQS + 1];  // deepest node covering i-1, i after boundary i
-    __shared__ int s_nlo[PLAN_MAX_SEQS], s_nhi[PLAN_MAX_SEQS], s_ndep[PLAN_MAX_SEQS], s_npar[PLAN_MAX_SEQS];
-    __shared__ int s_nid[PLAN_MAX_SEQS];      // node id of a representative boundary
-    __shared__ int s_brep[PLAN_MAX_SEQS], s_blo[PLAN_MAX_SEQS], s_bhi[PLAN_MAX_SEQS];  // per boundary
-    __shared__ int s_nbase[PLAN_MAX_SEQS], s_nchunk[PLAN_MAX_SEQS];
-    __shared__ int s_seg_units[2 * PLAN_MAX_SEQS];  // internal nodes, then leaves
-    __shared__ int s_seg_first[NKINDS][2 * PLAN_MAX_SEQS];  // first unit of each segment in its kind's queue
+    // per-sequence, per-boundary and per-node arrays in dynamic shared memory
+    // (plan_smem_bytes(n)); nodes and boundaries number at most n - 1
+    extern __shared__ int plan_smem[];
+    int* s_len = plan_smem;             // [n]
+    int* s_slot = s_len + n;            // [n]
+    int* s_h = s_slot + n;              // [n + 1] h[i] = LCP(i-1, i) in tokens, h[0] = h[n] = 0
+    int* s_top = s_h + n + 1;           // [n + 1] deepest node covering i-1, i after boundary i
+    int* s_nlo = s_top + n + 1;         // [n] node intervals, depths and parents
+    int* s_nhi = s_nlo + n;
+    int* s_ndep = s_nhi + n;
+    int* s_npar = s_ndep + n;
+    int* s_nid = s_npar + n;            // [n] node id of a representative boundary
+    int* s_brep = s_nid + n;            // [n] per boundary
+    int* s_blo = s_brep + n;
+    int* s_bhi = s_blo + n;
+    int* s_nbase = s_bhi + n;           // [n]
+    int* s_nchunk = s_nbase + n;        // [n]
+    int* s_seg_units = s_nchunk + n;    // [2n] internal nodes, then leaves
+    int* s_seg_first = s_seg_units + 2 * n;  // [NKINDS][2n] first unit of each segment in its kind's queue
     __shared__ int smem32[32];
     __shared__ int s_bcnt[LPT_BUCKETS];
     __shared__ long long s_scan64[32];
@@ -369,8 +388,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
         const int sh = 21 * kind;
         totals[kind] = (int)((ptot >> sh) & (FIELD - 1));
         const int e = (int)((pe >> sh) & (FIELD - 1));
-        if (s0 < nseg) s_seg_first[kind][s0] = e;
-        if (s1 < nseg) s_seg_first[kind][s1] = e + (int)((p0 >> sh) & (FIELD - 1));
+        if (s0 < nseg) s_seg_first[kind * 2 * n + s0] = e;
+        if (s1 < nseg) s_seg_first[kind * 2 * n + s1] = e + (int)((p0 >> sh) & (FIELD - 1));
     }
     if (tid == 0) {
         for (int kind = 0; kind < NKINDS; ++kind)
@@ -383,6 +402,10 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
         ws.hdr[HDR_NTCN] = s_err ? 0 : totals[KIND_TCN];
         ws.hdr[HDR_TCN_NEXT] = 0;
         ws.hdr[HDR_TC_ABORT] = 0;
+        ws.hdr[HDR_PLAN_N] = n;
+        ws.hdr[HDR_PLAN_PARTS] = max_parts;
+        ws.hdr[HDR_PLAN_G] = pp.G;
+        ws.hdr[HDR_PLAN_ROUTE] = plan_route(pp);
         if (s_err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, totals[0] + totals[1] + totals[2]);
     }
     __syncthreads();
@@ -393,7 +416,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     // CTA claims are the short ones.  Queue order does not change the result:
     // every unit writes its own (sequence, ordinal, head) partial.
     auto make_unit = [&](int kind, int u, int* rec) {
-        const int* first = s_seg_first[kind];
+        const int* first = s_seg_first + kind * 2 * n;
         int lo = 0, hi = nseg - 1;  // last segment whose first unit <= u (zero-count segments precede it)
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -477,6 +500,28 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __syncthreads();
     PLAN_TRACE(6);
     TL_LAST(3);
+}
+
+// ---------------------------------------------------------------------------
+// 1b. a call that reuses the plan in the workspace (another layer of the same
+//     decode step): check that the plan was made for this call's shape and
+//     routing, and restart the unit queues.  On a mismatch no unit runs, the
+//     merge zeroes the output and the call reports MENTAT_DEV_PLAN_OVERFLOW.
+// ---------------------------------------------------------------------------
+__global__ void k_plan_reuse(mentat_kv_cache c, int n, int max_parts, int route, int G, DecodeWs ws) {
+    griddep_wait();  // the previous call's merge has read the header
+    if (threadIdx.x == 0) {
+        const bool same = ws.hdr[HDR_PLAN_N] == n && ws.hdr[HDR_PLAN_PARTS] == max_parts &&
+                          ws.hdr[HDR_PLAN_G] == G && ws.hdr[HDR_PLAN_ROUTE] == route && ws.hdr[HDR_ERR] == 0;
+        if (!same) {
+            ws.hdr[HDR_ERR] = 1;
+            ws.hdr[HDR_NSIMT] = ws.hdr[HDR_NTC] = ws.hdr[HDR_NTCN] = 0;
+            set_error(c, MENTAT_DEV_PLAN_OVERFLOW, -1);
+        }
+        ws.hdr[HDR_SIMT_NEXT] = ws.hdr[HDR_TC_NEXT] = ws.hdr[HDR_TCN_NEXT] = 0;
+        ws.hdr[HDR_TC_ABORT] = 0;
+    }
+    griddep_launch();
 }
 
 // ---------------------------------------------------------------------------
@@ -788,7 +833,7 @@ static bool narrow_enabled() {
 template <typename T, int D>
 static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slots, int n, const void* q,
                          int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
-                         int max_parts, cudaStream_t s) {
+                         int max_parts, bool reuse_plan, cudaStream_t s) {
     const int G = Hq / c->num_kv_heads;
     const PoolMaps* maps = nullptr;
     bool tc_ok = false, narrow_ok = false;
@@ -817,14 +862,32 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows()};
     prof_mark(0, s);
     const bool pdl = pdl_enabled();
-    if (n > 1) {
-        if (launch(pdl, k_lcp, dim3(n - 1), dim3(LCP_THREADS), 0, s, *c, layer, slots, n, ws) != cudaSuccess)
+    if (reuse_plan) {
+        if (launch(pdl, k_plan_reuse, dim3(1), dim3(32), 0, s, *c, n, max_parts, plan_route(pp), G, ws) !=
+            cudaSuccess)
+            return MENTAT_ERR_CUDA;
+        MENTAT_CHECK_LAUNCH();
+    } else {
+        if (n > 1) {
+            if (launch(pdl, k_lcp, dim3(n - 1), dim3(LCP_THREADS), 0, s, *c, layer, slots, n, ws) != cudaSuccess)
+                return MENTAT_ERR_CUDA;
+            MENTAT_CHECK_LAUNCH();
+        }
+        // the plan's dynamic shared memory may exceed the default 48 KB (per-device attribute)
+        static bool plan_attr[64] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MENTAT_ERR_CUDA;
+        if (!plan_attr[dev]) {
+            if (cudaFuncSetAttribute(k_plan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     plan_smem_bytes(PLAN_MAX_SEQS)) != cudaSuccess)
+                return MENTAT_ERR_CUDA;
+            plan_attr[dev] = true;
+        }
+        if (launch(pdl, k_plan, dim3(1), dim3(1024), plan_smem_bytes(n), s, *c, layer, slots, n, pp, ws,
+                   max_parts) != cudaSuccess)
             return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
     }
-    if (launch(pdl, k_plan, dim3(1), dim3(1024), 0, s, *c, layer, slots, n, pp, ws, max_parts) != cudaSuccess)
-        return MENTAT_ERR_CUDA;
-    MENTAT_CHECK_LAUNCH();
     prof_mark(1, s);
     const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
     const T* qt = reinterpret_cast<const T*>(q);
@@ -919,9 +982,9 @@ int mentat_decode_set_wait_probe(int64_t cycles) {
     return MENTAT_OK;
 }
 
-int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n, const void* q,
+static int paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n, const void* q,
                         int64_t q_stride, int32_t Hq, void* out, int64_t out_stride, float scale, void* workspace,
-                        int64_t ws_bytes, int32_t max_parts, cudaStream_t s) {
+                        int64_t ws_bytes, int32_t max_parts, bool reuse_plan, cudaStream_t s) {
     if (!c || layer < 0 || layer >= c->num_layers || n < 0 || n > PLAN_MAX_SEQS || !c->k_pool || !c->v_pool ||
         Hq <= 0 || c->num_kv_heads <= 0 || Hq % c->num_kv_heads || max_parts <= 0)
         return MENTAT_ERR_ARG;
@@ -934,11 +997,13 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
     ws_carve(workspace, n, Hq, c->head_dim, max_parts, &w, &need);
     if (ws_bytes < need) return MENTAT_ERR_ARG;
     const int D = c->head_dim;
-#define MENTAT_DISPATCH(T)                                                                                  \
-    if (D == 128)                                                                                           \
-        return launch_decode<T, 128>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts, s); \
-    if (D == 64)                                                                                            \
-        return launch_decode<T, 64>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts, s);  \
+#define MENTAT_DISPATCH(T)                                                                                       \
+    if (D == 128)                                                                                                \
+        return launch_decode<T, 128>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts,  \
+                                     reuse_plan, s);                                                             \
+    if (D == 64)                                                                                                 \
+        return launch_decode<T, 64>(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, w, max_parts,   \
+                                    reuse_plan, s);                                                              \
     return MENTAT_ERR_UNSUPPORTED;
     switch (c->dtype) {
         case MENTAT_F32: { MENTAT_DISPATCH(float) }
@@ -947,6 +1012,21 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
         default: return MENTAT_ERR_UNSUPPORTED;
     }
 #undef MENTAT_DISPATCH
+}
+
+int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n, const void* q,
+                        int64_t q_stride, int32_t Hq, void* out, int64_t out_stride, float scale, void* workspace,
+                        int64_t ws_bytes, int32_t max_parts, cudaStream_t s) {
+    return paged_decode(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, workspace, ws_bytes,
+                        max_parts, false, s);
+}
+
+int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,
+                                   const void* q, int64_t q_stride, int32_t Hq, void* out, int64_t out_stride,
+                                   float scale, void* workspace, int64_t ws_bytes, int32_t max_parts,
+                                   cudaStream_t s) {
+    return paged_decode(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, workspace, ws_bytes,
+                        max_parts, true, s);
 }
 
 }  // extern "C"

@@ -29,6 +29,39 @@ constexpr int GATE_WARPS = GATE_THREADS / 32;
 
 template <typename T> __device__ __forceinline__ float rnd(float x) { return Elem<T>::to_f(Elem<T>::from_f(x)); }
 template <> __device__ __forceinline__ float rnd<float>(float x) { return x; }
+// bf16 round-to-nearest-even on the bit pattern (integer pipe; finite values and
+// infinities; the callers never pass NaN)
+template <> __device__ __forceinline__ float rnd<__nv_bfloat16>(float x) {
+    uint32_t u = __float_as_uint(x);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return __uint_as_float(u & 0xffff0000u);
+}
+
+// Correctly rounded a / b from rb = RN(1 / b) (Markstein's division, as in
+// P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 1990): q = RN(a rb) is within an ulp
+// of a / b, r = a - q b is exact with a fused multiply-add, and RN(q + r rb) is
+// the correctly rounded quotient, the same bits as IEEE division.  Quotients
+// near the underflow threshold (and a = 0) take the IEEE division itself.
+__device__ __forceinline__ float div_rn(float a, float b, float rb) {
+    const float q = __fmul_rn(a, rb);
+    if (!(fabsf(q) >= 0x1p-124f)) return __fdiv_rn(a, b);
+    const float r = __fmaf_rn(-q, b, a);
+    return __fmaf_rn(r, rb, q);
+}
+
+// Kahan's compensated sum in single precision (no reassociation: every step
+// is an explicit round-to-nearest operation); value() is the pair as a double
+struct KSum {
+    float s = 0.f, c = 0.f;
+    __device__ __forceinline__ void add(float x) {
+        const float y = __fsub_rn(x, c);
+        const float t = __fadd_rn(s, y);
+        c = __fsub_rn(__fsub_rn(t, s), y);
+        s = t;
+    }
+    __device__ __forceinline__ double value() const { return (double)s - (double)c; }
+};
 
 // 64-bit key ordering by value, then by lower index
 __device__ __forceinline__ uint64_t topkey(float v, int idx) {
@@ -89,29 +122,159 @@ __device__ __forceinline__ void warp_topk_merge(int K, Get get, uint64_t* dst) {
     }
 }
 
+// element u (a compile-time index after unrolling) of a 16-byte vector of T, as float
+template <typename T> __device__ __forceinline__ float vget(const uint4& r, int u);
+template <> __device__ __forceinline__ float vget<float>(const uint4& r, int u) { return __uint_as_float((&r.x)[u]); }
+template <> __device__ __forceinline__ float vget<__nv_bfloat16>(const uint4& r, int u) {
+    const uint32_t w = (&r.x)[u >> 1];
+    return __uint_as_float((u & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+template <> __device__ __forceinline__ float vget<__half>(const uint4& r, int u) {
+    const uint32_t w = (&r.x)[u >> 1];
+    return __half2float(__ushort_as_half((unsigned short)((u & 1) ? (w >> 16) : (w & 0xffffu))));
+}
+// element u of a 16-byte vector of T set to v (v is representable in T)
+template <typename T> __device__ __forceinline__ void vset(uint4& r, int u, float v);
+template <> __device__ __forceinline__ void vset<float>(uint4& r, int u, float v) { (&r.x)[u] = __float_as_uint(v); }
+template <> __device__ __forceinline__ void vset<__nv_bfloat16>(uint4& r, int u, float v) {
+    const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    uint32_t& w = (&r.x)[u >> 1];
+    w = (u & 1) ? ((w & 0xffffu) | (b << 16)) : ((w & 0xffff0000u) | b);
+}
+template <> __device__ __forceinline__ void vset<__half>(uint4& r, int u, float v) {
+    const uint32_t b = __half_as_ushort(__float2half_rn(v));
+    uint32_t& w = (&r.x)[u >> 1];
+    w = (u & 1) ? ((w & 0xffffu) | (b << 16)) : ((w & 0xffff0000u) | b);
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// online (max, sum exp, sum exp * shift) of the float-accurate entropy: the
+// state (m, S, A) stands for S = sum e^(y - m), A = sum e^(y - m) (y - m)
+struct AccEnt {
+    float m = -INFINITY, S = 0.f, A = 0.f;
+    __device__ __forceinline__ void add(float y) {
+        if (y > m) {
+            if (m != -INFINITY) {
+                const float f = expf(m - y);
+                A = (A + S * (m - y)) * f;
+                S *= f;
+            }
+            m = y;
+        }
+        const float d = y - m;
+        const float e = expf(d);
+        S += e;
+        A += e * d;
+    }
+    __device__ __forceinline__ void merge(float m2, float S2, float A2) {
+        if (m2 == -INFINITY) return;
+        if (m == -INFINITY) { m = m2; S = S2; A = A2; return; }
+        const float mn = fmaxf(m, m2);
+        const float f1 = expf(m - mn), f2 = expf(m2 - mn);
+        A = (A + S * (m - mn)) * f1 + (A2 + S2 * (m2 - mn)) * f2;
+        S = S * f1 + S2 * f2;
+        m = mn;
+    }
+    __device__ __forceinline__ void warp_merge() {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+            const float S2 = __shfl_xor_sync(0xffffffffu, S, o);
+            const float A2 = __shfl_xor_sync(0xffffffffu, A, o);
+            merge(m2, S2, A2);
+        }
+    }
+};
+
+// e^d for d <= 0 with IEEE single-precision multiplies and adds only (no fused
+// multiply-add, no hardware approximation), so that the numpy restatement in
+// the oracle produces the same bits.  Cody and Waite's argument reduction
+// (W. J. Cody, W. Waite, "Software Manual for the Elementary Functions", 1980):
+// d = k ln2 + r with k = rint(d / ln2), ln2 split into a 15-bit head (k ln2_hi
+// is exact) and a tail; then the degree-7 Taylor polynomial of e^r on
+// |r| <= ln2/2 by Horner's rule, and the exact scaling by 2^k (k rounded to the
+// nearest integer, ties to even, by the 1.5 * 2^23 addition).  Inputs below
+// -87 (results near the single-precision underflow) give 0.
+__device__ __forceinline__ float exp_cw(float d) {
+    if (!(d >= -87.0f)) return 0.0f;
+    // k = rint(d log2(e)): adding 1.5 * 2^23 rounds to an integer (ties to even)
+    // and leaves it in the low bits of the sum
+    const float kb = __fadd_rn(__fmul_rn(d, 0x1.715476p+0f), 12582912.0f);
+    const float k = __fsub_rn(kb, 12582912.0f);
+    const int ki = __float_as_int(kb) - 0x4b400000;
+    const float r = __fsub_rn(__fsub_rn(d, __fmul_rn(k, 0x1.62e4p-1f)),  // ln2 head
+                              __fmul_rn(k, 0x1.7f7d1cp-20f));            // ln2 tail
+    float p = 0x1.a01a02p-13f;                                           // 1/7!
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.6c16c2p-10f);                     // 1/6!
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.111112p-7f);                      // 1/5!
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-5f);                      // 1/4!
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-3f);                      // 1/3!
+    p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+    p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+    p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+    return __fmul_rn(p, __int_as_float((ki + 127) << 23));                // k >= -126
+}
+
+// Inserts `cur` into the descending list best[0..K); returns the new best[K - 1].
+// Out of line, so that the list lives in local memory and the hot loop keeps
+// only the threshold in registers.
+__device__ __noinline__ uint64_t topk_insert(uint64_t* best, int K, uint64_t cur) {
+    for (int k = 0; k < K; ++k) {
+        if (cur > best[k]) {
+            const uint64_t t = best[k];
+            best[k] = cur;
+            cur = t;
+        }
+    }
+    return best[K - 1];
+}
+
+// Dynamic shared memory of a gate CTA: the slice's repetition-penalty bitmap,
+// then (when `cache` is set) the slice's xt and z values in the logits dtype,
+// which passes B and C read instead of the logits.
+template <typename T>
+__host__ __device__ inline int gate_slice(int V) {
+    return ((V + GATE_CLUSTER - 1) / GATE_CLUSTER + GATE_VEC - 1) / GATE_VEC * GATE_VEC;
+}
+__host__ __device__ inline int gate_bitmap_bytes(int per) { return ((per + 31) / 32 * 4 + 15) / 16 * 16; }
+
 template <typename T>
 __global__ void __launch_bounds__(GATE_THREADS, sizeof(T) == 4 ? 1 : 2)  // fp32 needs > 64 registers
 k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restrict__ hist_ptr,
        const int32_t* __restrict__ hist_ids, const double* __restrict__ ema_old, mentat_gate_params P,
-       mentat_gate_out* __restrict__ out) {
+       mentat_gate_out* __restrict__ out, int cache) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ uint32_t bitmap[];
-    __shared__ float s_red[4][GATE_WARPS];
+    extern __shared__ __align__(16) uint8_t gate_smem[];
+    __shared__ float s_red[2][GATE_WARPS], s_acc[3][GATE_WARPS];
+    __shared__ double s_redd[2][GATE_WARPS];
     __shared__ uint64_t s_keys[GATE_WARPS][MENTAT_GATE_MAXK];
-    __shared__ float s_xa[2], s_xb[4], s_xc[2];      // this CTA's values of passes A, B, C
+    __shared__ float s_xa[5];                        // this CTA's values of pass A
+    __shared__ double s_xb[2], s_xc[2];              // ... of passes B and C
     __shared__ uint64_t s_xk[MENTAT_GATE_MAXK];      // this CTA's top-K
-    __shared__ float s_glob[6];
+    __shared__ float s_glob[5];
+    __shared__ double s_globd[2];
     const int C = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int leaf = blockIdx.x / C, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = ((V + C - 1) / C + GATE_VEC - 1) / GATE_VEC * GATE_VEC;
+    const int per = gate_slice<T>(V);
     const int v0 = min(V, rank * per), v1 = min(V, v0 + per);
     const int nwords = (per + 31) >> 5;
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(gate_smem);
+    T* xt_s = reinterpret_cast<T*>(gate_smem + gate_bitmap_bytes(per));  // [per]
+    T* z_s = xt_s + per;                                                // [per]
     const T* x = logits + (int64_t)leaf * ld;
     const float Tf = (float)P.temperature, pf = (float)P.penalty;
+    const float rT = __frcp_rn(Tf), rP = __frcp_rn(pf);  // correctly rounded reciprocals for div_rn
+    const bool want_pen = (P.flags & MENTAT_GATE_SKIP_PEN_ENTROPY) == 0;
     const bool use_t = P.temperature != 1.0;
     const int K = P.K;
     const bool vec = ((reinterpret_cast<uintptr_t>(x) | (uintptr_t)(v0 * sizeof(T))) & 15) == 0;
+    constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
 
     for (int w = tid; w < nwords; w += GATE_THREADS) bitmap[w] = 0u;
     __syncthreads();
@@ -120,147 +283,196 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
         if (id >= v0 && id < v1) atomicOr(&bitmap[(id - v0) >> 5], 1u << ((id - v0) & 31));
     }
     __syncthreads();
-    // f(i, x_i, xt_i, z_i, y_i) for every element of the slice: vector steps, then the tail
-    auto for_slice = [&](auto&& f) {
+    // f(i, xt_i, z_i, y_i) for every element of the slice, from the logits:
+    // y = x / T, xt = R(y), z = the penalised logit
+    auto from_logits = [&](auto&& f) {
         auto elem = [&](int i, float xv, uint32_t hit) {
-            const float y = use_t ? xv / Tf : xv;
+            const float y = use_t ? div_rn(xv, Tf, rT) : xv;
             const float xt = use_t ? rnd<T>(y) : xv;
             float z = xv;
-            if (hit) z = xv > 0.f ? rnd<T>(xv / pf) : rnd<T>(xv * pf);
+            if (hit) z = xv > 0.f ? rnd<T>(div_rn(xv, pf, rP)) : rnd<T>(__fmul_rn(xv, pf));
             f(i, xt, z, y);
         };
         int tail = v0;
         if (vec) {
-            constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
             for (int j = v0 + tid * VW; j + VW <= v1; j += GATE_THREADS * VW) {
-                alignas(16) T e[VW];
-                *reinterpret_cast<uint4*>(e) = *reinterpret_cast<const uint4*>(x + j);
+                const uint4 e = *reinterpret_cast<const uint4*>(x + j);
                 const uint32_t bits = bitmap[(j - v0) >> 5] >> ((j - v0) & 31);
 #pragma unroll
-                for (int u = 0; u < VW; ++u) elem(j + u, Elem<T>::to_f(e[u]), (bits >> u) & 1u);
+                for (int u = 0; u < VW; ++u) elem(j + u, vget<T>(e, u), (bits >> u) & 1u);
             }
             tail = v0 + (v1 - v0) / VW * VW;
         }
         for (int i = tail + tid; i < v1; i += GATE_THREADS)
             elem(i, Elem<T>::to_f(x[i]), (bitmap[(i - v0) >> 5] >> ((i - v0) & 31)) & 1u);
     };
+    // g(i, xt_i, z_i) for every element of the slice: from the shared-memory
+    // copy when the slice is cached, else recomputed from the logits
+    auto for_slice = [&](auto&& g) {
+        if (cache) {
+            const int n = v1 - v0;
+            for (int j = tid * VW; j + VW <= n; j += GATE_THREADS * VW) {
+                const uint4 a = *reinterpret_cast<const uint4*>(xt_s + j);
+                const uint4 b = *reinterpret_cast<const uint4*>(z_s + j);
+#pragma unroll
+                for (int u = 0; u < VW; ++u) g(v0 + j + u, vget<T>(a, u), vget<T>(b, u));
+            }
+            for (int i = n / VW * VW + tid; i < n; i += GATE_THREADS)
+                g(v0 + i, Elem<T>::to_f(xt_s[i]), Elem<T>::to_f(z_s[i]));
+        } else {
+            from_logits([&](int i, float xt, float z, float) { g(i, xt, z); });
+        }
+    };
 
-    // pass A: maxima
+    // pass A: maxima of xt and z, the float-accurate entropy's online sums, and
+    // the slice copy (16-byte stores when the logits were read 16 bytes at a time)
     float mt = -INFINITY, mz = -INFINITY;
-    for_slice([&](int, float xt, float z, float) {
+    AccEnt acc;
+    auto take = [&](float xt, float z, float y) {
         mt = fmaxf(mt, xt);
         mz = fmaxf(mz, z);
-    });
+        acc.add(y);
+    };
+    if (vec && cache) {
+        for (int j = v0 + tid * VW; j + VW <= v1; j += GATE_THREADS * VW) {
+            const uint4 e = *reinterpret_cast<const uint4*>(x + j);
+            uint4 a = e, b = e;
+            const uint32_t bits = bitmap[(j - v0) >> 5] >> ((j - v0) & 31);
+#pragma unroll
+            for (int u = 0; u < VW; ++u) {
+                const float xv = vget<T>(e, u);
+                const float y = use_t ? div_rn(xv, Tf, rT) : xv;
+                const float xt = use_t ? rnd<T>(y) : xv;
+                float z = xv;
+                if ((bits >> u) & 1u) z = xv > 0.f ? rnd<T>(div_rn(xv, pf, rP)) : rnd<T>(__fmul_rn(xv, pf));
+                take(xt, z, y);
+                if (use_t) vset<T>(a, u, xt);
+                if ((bits >> u) & 1u) vset<T>(b, u, z);
+            }
+            *reinterpret_cast<uint4*>(xt_s + (j - v0)) = a;
+            *reinterpret_cast<uint4*>(z_s + (j - v0)) = b;
+        }
+        const int tail = v0 + (v1 - v0) / VW * VW;
+        for (int i = tail + tid; i < v1; i += GATE_THREADS) {
+            const float xv = Elem<T>::to_f(x[i]);
+            const float y = use_t ? div_rn(xv, Tf, rT) : xv;
+            const float xt = use_t ? rnd<T>(y) : xv;
+            float z = xv;
+            if ((bitmap[(i - v0) >> 5] >> ((i - v0) & 31)) & 1u) z = xv > 0.f ? rnd<T>(div_rn(xv, pf, rP)) : rnd<T>(__fmul_rn(xv, pf));
+            take(xt, z, y);
+            xt_s[i - v0] = Elem<T>::from_f(xt);
+            z_s[i - v0] = Elem<T>::from_f(z);
+        }
+    } else {
+        from_logits([&](int i, float xt, float z, float y) {
+            take(xt, z, y);
+            if (cache) {
+                xt_s[i - v0] = Elem<T>::from_f(xt);
+                z_s[i - v0] = Elem<T>::from_f(z);
+            }
+        });
+    }
+    __syncthreads();  // the slice copy is read by other threads in passes B and C
     mt = warp_maxf(mt);
     mz = warp_maxf(mz);
+    acc.warp_merge();
     if (lane == 0) { s_red[0][warp] = mt; s_red[1][warp] = mz; }
+    if (lane == 0) { s_acc[0][warp] = acc.m; s_acc[1][warp] = acc.S; s_acc[2][warp] = acc.A; }
     __syncthreads();
     if (warp == 0) {
         const float a = warp_maxf(lane < GATE_WARPS ? s_red[0][lane] : -INFINITY);
         const float b = warp_maxf(lane < GATE_WARPS ? s_red[1][lane] : -INFINITY);
-        if (lane == 0) { s_xa[0] = a; s_xa[1] = b; }
+        AccEnt t;
+        if (lane < GATE_WARPS) t.merge(s_acc[0][lane], s_acc[1][lane], s_acc[2][lane]);
+        t.warp_merge();
+        if (lane == 0) { s_xa[0] = a; s_xa[1] = b; s_xa[2] = t.m; s_xa[3] = t.S; s_xa[4] = t.A; }
     }
     cluster.sync();
     if (warp == 0) {
         float a = -INFINITY, b = -INFINITY;
+        AccEnt t;
         if (lane < C) {
             const float* r = cluster.map_shared_rank(s_xa, lane);
             a = r[0];
             b = r[1];
+            t.merge(r[2], r[3], r[4]);
         }
         a = warp_maxf(a);
         b = warp_maxf(b);
-        if (lane == 0) { s_glob[0] = a; s_glob[1] = b; }
+        t.warp_merge();
+        if (lane == 0) { s_glob[0] = a; s_glob[1] = b; s_glob[2] = t.S; s_glob[3] = t.A; }
     }
     __syncthreads();
     mt = s_glob[0];
     mz = s_glob[1];
 
-    // pass B: sums of exp about the maxima (the accurate entropy's shifted by mt)
-    float St = 0.f, Sz = 0.f, Sa = 0.f, Aa = 0.f;
-    for_slice([&](int, float xt, float z, float y) {
-        St += expf(xt - mt);
-        Sz += expf(z - mz);
-        const float d = y - mt;
-        const float ea = expf(d);
-        Sa += ea;
-        Aa += ea * d;
+    // pass B: S = sum exp(xt - mt) and the penalised one, accumulated in double
+    // and rounded to float once: the float sum of the reference, exactly rounded
+    KSum kt, kz;
+    for_slice([&](int, float xt, float z) {
+        kt.add(exp_cw(__fsub_rn(xt, mt)));
+        kz.add(exp_cw(__fsub_rn(z, mz)));
     });
-    St = warp_sum(St);
-    Sz = warp_sum(Sz);
-    Sa = warp_sum(Sa);
-    Aa = warp_sum(Aa);
-    if (lane == 0) { s_red[0][warp] = St; s_red[1][warp] = Sz; s_red[2][warp] = Sa; s_red[3][warp] = Aa; }
+    double St = warp_sum_d(kt.value());
+    double Sz = warp_sum_d(kz.value());
+    if (lane == 0) { s_redd[0][warp] = St; s_redd[1][warp] = Sz; }
     __syncthreads();
     if (warp == 0) {
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = warp_sum(lane < GATE_WARPS ? s_red[k][lane] : 0.f);
-        if (lane == 0) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) s_xb[k] = v[k];
-        }
+        const double a = warp_sum_d(lane < GATE_WARPS ? s_redd[0][lane] : 0.0);
+        const double b = warp_sum_d(lane < GATE_WARPS ? s_redd[1][lane] : 0.0);
+        if (lane == 0) { s_xb[0] = a; s_xb[1] = b; }
     }
     cluster.sync();
     if (warp == 0) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        double a = 0.0, b = 0.0;
         if (lane < C) {
-            const float* r = cluster.map_shared_rank(s_xb, lane);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = r[k];
+            const double* r = cluster.map_shared_rank(s_xb, lane);
+            a = r[0];
+            b = r[1];
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = warp_sum(v[k]);
-        if (lane == 0) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) s_glob[2 + k] = v[k];
-        }
+        a = warp_sum_d(a);
+        b = warp_sum_d(b);
+        if (lane == 0) { s_globd[0] = a; s_globd[1] = b; }
     }
     __syncthreads();
-    St = s_glob[2];
-    Sz = s_glob[3];
-    const float Lt = rnd<T>(logf(rnd<T>(St)));
-    const float Lz = rnd<T>(logf(rnd<T>(Sz)));
+    const float Stf = (float)s_globd[0], Szf = (float)s_globd[1];
+    const float rSt = __frcp_rn(Stf), rSz = __frcp_rn(Szf);
+    // log in double, rounded once to float: the correctly rounded value
+    // log-softmax = (x - m) - L.  torch's CPU kernels take L = R(log(R(S))) (the
+    // default); with MENTAT_GATE_FLOAT_LOGSUM, L = log(S) in float, as its CUDA
+    // kernels do.  The logs are correctly rounded (double, rounded once).
+    const bool float_logsum = (P.flags & MENTAT_GATE_FLOAT_LOGSUM) != 0;
+    const float Lt = float_logsum ? (float)log((double)Stf) : rnd<T>((float)log((double)rnd<T>(Stf)));
+    const float Lz = float_logsum ? (float)log((double)Szf) : rnd<T>((float)log((double)rnd<T>(Szf)));
 
-    // pass C: rounded entropies and the top-K of the penalised log-probs
-    float Hs = 0.f, Hz = 0.f;
+    // pass C: rounded entropies (terms summed in double) and the top-K of the
+    // penalised log-probs
+    KSum hs, hz;
     uint64_t best[MENTAT_GATE_MAXK];
 #pragma unroll
     for (int k = 0; k < MENTAT_GATE_MAXK; ++k) best[k] = 0ull;
     uint64_t kth = 0ull;  // best[K - 1], the smallest key kept
-    for_slice([&](int i, float xt, float z, float) {
+    for_slice([&](int i, float xt, float z) {
         {
-            const float p = rnd<T>(expf(xt - mt) / St);
-            const float lp = rnd<T>((xt - mt) - Lt);
-            float pl = rnd<T>(p * lp);
-            if (pl != pl) pl = 0.f;
-            Hs += pl;
+            const float dt = __fsub_rn(xt, mt);
+            const float p = rnd<T>(div_rn(exp_cw(dt), Stf, rSt));
+            const float lp = rnd<T>(__fsub_rn(dt, Lt));
+            const float pl = __fmul_rn(p, lp);
+            if (pl == pl) hs.add(rnd<T>(pl));  // nan_to_num: NaN terms count as 0
         }
-        const float lpz = rnd<T>((z - mz) - Lz);
-        {
-            const float p = rnd<T>(expf(z - mz) / Sz);
-            float pl = rnd<T>(p * lpz);
-            if (pl != pl) pl = 0.f;
-            Hz += pl;
+        const float dz = __fsub_rn(z, mz);
+        const float lpz = rnd<T>(__fsub_rn(dz, Lz));
+        if (want_pen) {
+            const float p = rnd<T>(div_rn(exp_cw(dz), Szf, rSz));
+            const float pl = __fmul_rn(p, lpz);
+            if (pl == pl) hz.add(rnd<T>(pl));
         }
-        uint64_t cur = topkey(lpz, i);
-        if (cur > kth) {
-#pragma unroll
-            for (int k = 0; k < MENTAT_GATE_MAXK; ++k) {
-                if (k < K && cur > best[k]) {
-                    const uint64_t t = best[k];
-                    best[k] = cur;
-                    cur = t;
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < MENTAT_GATE_MAXK; ++k)
-                if (k == K - 1) kth = best[k];
-        }
+        const uint64_t cur = topkey(lpz, i);
+        if (cur > kth) kth = topk_insert(best, K, cur);  // rare once the list has filled
     });
-    Hs = warp_sum(Hs);
-    Hz = warp_sum(Hz);
-    if (lane == 0) { s_red[0][warp] = Hs; s_red[1][warp] = Hz; }
+    const double Hs = warp_sum_d(hs.value());
+    const double Hz = warp_sum_d(hz.value());
+    if (lane == 0) { s_redd[0][warp] = Hs; s_redd[1][warp] = Hz; }
     warp_topk_merge(K, [&](int head) {
         uint64_t v = 0ull;
 #pragma unroll
@@ -270,8 +482,8 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
     }, s_keys[warp]);
     __syncthreads();
     if (warp == 0) {
-        const float a = warp_sum(lane < GATE_WARPS ? s_red[0][lane] : 0.f);
-        const float b = warp_sum(lane < GATE_WARPS ? s_red[1][lane] : 0.f);
+        const double a = warp_sum_d(lane < GATE_WARPS ? s_redd[0][lane] : 0.0);
+        const double b = warp_sum_d(lane < GATE_WARPS ? s_redd[1][lane] : 0.0);
         warp_topk_merge(K, [&](int head) {
             return lane < GATE_WARPS && head < K ? s_keys[lane][head] : 0ull;
         }, s_xk);
@@ -279,25 +491,25 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
     }
     cluster.sync();
     if (rank == 0 && warp == 0) {  // the leaf's sums, top-K and decision
-        float a = 0.f, b = 0.f;
+        double a = 0.0, b = 0.0;
         const uint64_t* rk = nullptr;
         if (lane < C) {
-            const float* r = cluster.map_shared_rank(s_xc, lane);
+            const double* r = cluster.map_shared_rank(s_xc, lane);
             a = r[0];
             b = r[1];
             rk = cluster.map_shared_rank(s_xk, lane);
         }
-        a = warp_sum(a);
-        b = warp_sum(b);
+        a = warp_sum_d(a);
+        b = warp_sum_d(b);
         warp_topk_merge(K, [&](int head) { return lane < C && head < K ? rk[head] : 0ull; }, s_keys[0]);
         __syncwarp();
         if (lane == 0) {
             const uint64_t* res = s_keys[0];
             mentat_gate_out o;
-            const double H = -(double)rnd<T>(a);
+            const double H = -(double)rnd<T>((float)a);
             o.entropy = H;
-            o.pen_entropy = -(double)rnd<T>(b);
-            o.entropy_acc = (double)logf(s_glob[4]) - (double)s_glob[5] / (double)s_glob[4];
+            o.pen_entropy = want_pen ? -(double)rnd<T>((float)b) : 0.0;
+            o.entropy_acc = (double)logf(s_glob[2]) - (double)s_glob[3] / (double)s_glob[2];
             const double eo = ema_old[leaf];
             double ema;
             if (eo != eo) ema = H;
@@ -327,12 +539,27 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
     cluster.sync();  // every CTA's shared memory stays alive until rank 0 has read it
 }
 
+// shared memory a CTA may hold: the whole slice cache when it fits
+constexpr int GATE_SMEM_MAX = 200 * 1024;
+
 template <typename T>
 static int launch_gate(const void* logits, int n, int V, int64_t ld, const int32_t* hp, const int32_t* hi,
                        const double* ema, const mentat_gate_params& P, mentat_gate_out* out, cudaStream_t s) {
-    const int per = ((V + GATE_CLUSTER - 1) / GATE_CLUSTER + GATE_VEC - 1) / GATE_VEC * GATE_VEC;
-    const size_t smem = (size_t)((per + 31) / 32) * 4;
-    // V <= 2^20 keeps the slice bitmap within 16 KB, under the default dynamic limit
+    const int per = gate_slice<T>(V);
+    const size_t bm = (size_t)gate_bitmap_bytes(per);
+    const size_t cached = bm + (size_t)2 * per * sizeof(T);
+    const int cache = cached <= (size_t)GATE_SMEM_MAX ? 1 : 0;
+    const size_t smem = cache ? cached : bm;  // V <= 2^20 keeps the bitmap alone within 16 KB
+    // the dynamic shared-memory limit is a per-device attribute
+    static bool attr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MENTAT_ERR_CUDA;
+    if (!attr[dev]) {
+        if (cudaFuncSetAttribute(k_gate<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, GATE_SMEM_MAX) !=
+            cudaSuccess)
+            return MENTAT_ERR_CUDA;
+        attr[dev] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n * GATE_CLUSTER);
     cfg.blockDim = dim3(GATE_THREADS);
@@ -345,8 +572,8 @@ static int launch_gate(const void* logits, int n, int V, int64_t ld, const int32
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, k_gate<T>, reinterpret_cast<const T*>(logits), V, ld, hp, hi, ema, P, out) !=
-        cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, k_gate<T>, reinterpret_cast<const T*>(logits), V, ld, hp, hi, ema, P, out,
+                           cache) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     return MENTAT_OK;

@@ -20,7 +20,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import _lib, ops  # noqa: F401  (ops registers torch.ops.mentat_b200.gate_step)
+from . import _lib, ops
 
 _DT = {torch.bfloat16: _lib.MENTAT_BF16, torch.float16: _lib.MENTAT_F16, torch.float32: _lib.MENTAT_F32}
 
@@ -44,6 +44,13 @@ class GateConfig:
     branching_factor: int = 3
     max_active_branches: int = 10
     soft_explore_window: int = 10
+    # the penalised entropy serves only the reference's branch-point diagnostics
+    # (generator.py:291-293); False leaves it out of the kernel (0 in the record)
+    pen_entropy: bool = True
+    # log-softmax rounding: "cpu" rounds log(sum) to the logits dtype as torch's
+    # CPU kernels do (pinned by the golden fixtures); "cuda" keeps it in float as
+    # torch's CUDA kernels do
+    log_softmax: str = "cpu"
 
 
 class Gate:
@@ -92,11 +99,13 @@ class Gate:
         self._ema_dev[:n].copy_(self._ema_host[:n], non_blocking=True)
         c = self.cfg
         nb = n * GATE_OUT_DTYPE.itemsize
-        torch.ops.mentat_b200.gate_step(
+        ops.gate_step(
             logits, self._ptr_dev[: n + 1], self._hist_dev, self._ema_dev[:n],
             [c.temperature, c.repetition_penalty, c.entropy_ema_alpha, c.relative_entropy_multiplier,
              c.soft_explore_initial],
-            [c.branching_factor, c.max_active_branches, num_active, step, c.soft_explore_window],
+            [c.branching_factor, c.max_active_branches, num_active, step, c.soft_explore_window,
+             (0 if c.pen_entropy else _lib.GATE_SKIP_PEN_ENTROPY)
+             | (_lib.GATE_FLOAT_LOGSUM if c.log_softmax == "cuda" else 0)],
             self._out_dev[:nb])
         self._out_host[:nb].copy_(self._out_dev[:nb], non_blocking=True)
         self._n = n

@@ -431,7 +431,7 @@ class PagedKVCacheManager:
                 s.tokens_in_last_block[L] = tf + 1
             s.num_tokens[L] += 1
         slots = self._slots_dev(seq_ids)
-        torch.ops.mentat_b200.append_batched(self._k_all, self._v_all, slots, k, v, self._op_id, layer_idx)
+        ops.append_batched(self._k_all, self._v_all, slots, k, v, self._op_id, layer_idx)
         self._after()
 
     def get_kv_length(self, seq_id: int) -> int:            # :285-287

@@ -36,7 +36,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-from . import _lib
+from . import _lib, ops
 from .attention_backend import attn_decode, attn_prefill
 from .gate import Gate, GateConfig
 from .paged_kv_cache import PagedKVCacheManager
@@ -271,8 +271,10 @@ class PagedLM:
             attn = blk.self_attn
             q, k, v = self._qkv(attn, blk.input_layernorm(h), (N,))
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
-            torch.ops.mentat_b200.append_batched(c._k_all, c._v_all, slots, k, v, c._op_id, layer_idx)
-            o = torch.ops.mentat_b200.paged_decode(q, dec_slots, self._graph_max_len, c._op_id, layer_idx, scale)
+            ops.append_batched(c._k_all, c._v_all, slots, k, v, c._op_id, layer_idx)
+            # every layer has the tree's sharing structure: plan once per step
+            o = ops.paged_decode(q, dec_slots, self._graph_max_len, c._op_id, layer_idx, scale,
+                                 reuse_plan=layer_idx > 0)
             h = h + self._sum(attn.o_proj(o.reshape(N, -1)))
             h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         h = self.norm(h)
@@ -434,7 +436,7 @@ class TreeRollout:
                  soft_explore_initial: float = 0.3, max_seqs: int = 256, cuda_graphs: bool = True,
                  max_prompt_len: int = 4096, entropy_threshold: Optional[float] = None,
                  max_blocks_per_seq: Optional[int] = None, static_decode: bool = False, tp_group=None,
-                 graph_bucket: Optional[int] = None):
+                 graph_bucket: Optional[int] = None, log_softmax: str = "cpu"):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -452,7 +454,9 @@ class TreeRollout:
                                    entropy_ema_alpha=entropy_ema_alpha,
                                    relative_entropy_multiplier=relative_entropy_multiplier,
                                    soft_explore_initial=soft_explore_initial, branching_factor=branching_factor,
-                                   max_active_branches=max_active_branches, soft_explore_window=soft_explore_window)
+                                   max_active_branches=max_active_branches, soft_explore_window=soft_explore_window,
+                                   pen_entropy=False,  # only the reference's diagnostics use it
+                                   log_softmax=log_softmax)
         self.device = dev
         self.cuda_graphs = cuda_graphs
         self.static_decode = static_decode  # without graphs: plan on the device, no per-layer host work
@@ -468,6 +472,7 @@ class TreeRollout:
         self.decode_time_s = 0.0
         self.steps = 0
         self.step_leaves = []        # sequences decoded at each step
+        self.trace = None            # when a list: each step's active leaves (generated ids), per tree
 
     # ---- per-leaf decision (generator.py:250-374) ---------------------------
     def _records(self, recs) -> list:
@@ -581,6 +586,8 @@ class TreeRollout:
                 break
             self.steps += 1
             self.step_leaves.append(len(leaves))
+            if self.trace is not None:
+                self.trace.append([sorted(lf.seq for lf in lv) for lv in per_tree])
             tokens = torch.tensor([lf.token_ids[-1] for lf in leaves], dtype=torch.long).to(self.device,
                                                                                               non_blocking=True)
             logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])

@@ -60,27 +60,70 @@ def _sum_f32(a: np.ndarray) -> np.float32:
     return np.float32(np.sum(a, dtype=np.float64))
 
 
-def softmax_parts(xt: np.ndarray):
-    """(m, e, S, L) of the bf16 softmax / log_softmax of bf16 values ``xt``."""
+_F = np.float32
+
+
+def _hexf(h: str) -> np.float32:
+    return np.float32(float.fromhex(h))  # the literals are exact float32 values
+
+
+_LOG2E, _LN2_HI, _LN2_LO = _hexf("0x1.715476p+0"), _hexf("0x1.62e4p-1"), _hexf("0x1.7f7d1cp-20")
+_EXP_POLY = [_hexf(h) for h in ("0x1.a01a02p-13", "0x1.6c16c2p-10", "0x1.111112p-7", "0x1.555556p-5",
+                                "0x1.555556p-3")] + [_F(0.5), _F(1.0), _F(1.0)]
+
+
+def exp_cw(d) -> np.ndarray:
+    """e^d (d <= 0) in IEEE float32 multiplies and adds only: Cody and Waite's
+    argument reduction (Cody, Waite, "Software Manual for the Elementary
+    Functions", 1980; k = rint(d / ln2) by adding 1.5 * 2^23) and the degree-7
+    Taylor polynomial of e^r, exactly the operations of the CUDA gate kernel's
+    ``exp_cw``, so both give the same bits.
+    The reference's torch CPU softmax uses its own vectorised expf; the two
+    differ by about an ulp on some elements, which can move a probability
+    across a bf16 rounding boundary (the residual mismatch the tests measure).
+    Inputs below -87 give 0."""
+    d = np.asarray(d, np.float32)
+    ok = d >= _F(-87.0)
+    d = np.where(ok, d, _F(0))
+    # k = rint(d log2(e)): adding 1.5 * 2^23 rounds to an integer, ties to even
+    kb = (d * _LOG2E + _F(12582912.0)).astype(np.float32)
+    k = (kb - _F(12582912.0)).astype(np.float32)
+    ki = kb.view(np.int32) - np.int32(0x4B400000)
+    r = ((d - k * _LN2_HI) - k * _LN2_LO).astype(np.float32)
+    p = _EXP_POLY[0]
+    for c in _EXP_POLY[1:]:
+        p = (p * r + c).astype(np.float32)
+    scale = ((ki + 127) << 23).astype(np.int32).view(np.float32)
+    return np.where(ok, (p * scale).astype(np.float32), _F(0)).astype(np.float32)
+
+
+def softmax_parts(xt: np.ndarray, float_logsum: bool = False):
+    """(m, e, S, L) of the bf16 softmax / log_softmax of bf16 values ``xt``:
+    e = exp(xt - m) (float32), S = the float32 rounding of the exact sum of e,
+    L = bf16(log(bf16(S))) with log correctly rounded to float32 (torch's CPU
+    log_softmax), or L = log(S) in float32 with ``float_logsum`` (its CUDA one)."""
     m = np.float32(xt.max())
     with np.errstate(invalid="ignore", over="ignore"):
-        e = np.exp((xt - m).astype(np.float32)).astype(np.float32)
+        e = exp_cw((xt - m).astype(np.float32))
     S = _sum_f32(e)
-    L = bf16_round(np.float32(np.log(bf16_round(S)[()])))[()]
+    if float_logsum:
+        L = np.float32(np.log(np.float64(S)))
+    else:
+        L = bf16_round(np.float32(np.log(np.float64(bf16_round(S)[()]))))[()]
     return m, e, S, np.float32(L)
 
 
-def log_softmax_bf16(z: np.ndarray) -> np.ndarray:
-    m, _, _, L = softmax_parts(z)
+def log_softmax_bf16(z: np.ndarray, float_logsum: bool = False) -> np.ndarray:
+    m, _, _, L = softmax_parts(z, float_logsum)
     with np.errstate(invalid="ignore"):
         return bf16_round((z - m).astype(np.float32) - L)
 
 
-def entropy_bf16(x: np.ndarray, temperature: float = 1.0) -> float:
+def entropy_bf16(x: np.ndarray, temperature: float = 1.0, float_logsum: bool = False) -> float:
     """``compute_entropy`` (``generator_utils.py:196-202``); x holds bf16 values."""
     x = np.asarray(x, np.float32)
     xt = bf16_round(x / np.float32(temperature)) if temperature != 1.0 else x.copy()
-    m, e, S, L = softmax_parts(xt)
+    m, e, S, L = softmax_parts(xt, float_logsum)
     with np.errstate(invalid="ignore", divide="ignore"):
         p = bf16_round(e / S)
         lp = bf16_round((xt - m).astype(np.float32) - L)
@@ -151,15 +194,16 @@ def decide(entropy: float, ema_old, *, alpha, mult, M, num_active, K, step,
 
 
 def gate_leaf(x, history, *, temperature, penalty, K, ema_old, alpha, mult, M,
-              num_active, step, window, initial):
-    """Everything ``_step_leaf`` computes for one leaf."""
+              num_active, step, window, initial, float_logsum=False):
+    """Everything ``_step_leaf`` computes for one leaf (``float_logsum``: the
+    log-softmax rounding of torch's CUDA kernels instead of its CPU ones)."""
     x = np.asarray(x, np.float32)
-    H = entropy_bf16(x, temperature)
+    H = entropy_bf16(x, temperature, float_logsum)
     branch, ema, tau = decide(H, ema_old, alpha=alpha, mult=mult, M=M,
                               num_active=num_active, K=K, step=step,
                               window=window, initial=initial)
     z = apply_penalty(x, history, penalty)
-    lp = log_softmax_bf16(z)
+    lp = log_softmax_bf16(z, float_logsum)
     am = argmax_lowest(lp)
     tk, tv = topk_lowest(lp, K)
     return {
@@ -172,5 +216,5 @@ def gate_leaf(x, history, *, temperature, penalty, K, ema_old, alpha, mult, M,
         "argmax_lp": float(lp[am]),
         "topk_ids": tk.tolist(),
         "topk_lps": [float(v) for v in tv],
-        "pen_entropy": entropy_bf16(z, 1.0),
+        "pen_entropy": entropy_bf16(z, 1.0, float_logsum),
     }

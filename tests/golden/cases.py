@@ -199,7 +199,62 @@ def rollout_model(c, device="cpu"):
     return model.to(device=device, dtype=torch.float32).eval()
 
 
+def sharpen(model, factor: float = 40.0):
+    """The model with its lm_head (untied from the embedding) scaled by ``factor``.
+
+    A tiny random-init model has nearly uniform next-token distributions; in
+    bf16 its top log-probs are then mostly exact ties, whose order torch.topk
+    leaves implementation-defined, so bf16 trees would part on tie order alone.
+    Sharper logits keep the bf16 comparisons about the arithmetic."""
+    import torch
+    model.lm_head.weight = torch.nn.Parameter(model.lm_head.weight.detach().clone() * factor)
+    return model
+
+
 def rollout_prompts(c):
     rng = np.random.default_rng(c["seed"] + 1000)
     # ids >= 4 keep the prompt clear of the EOS id
     return [rng.integers(4, c["vocab"], c["prompt_len"]).tolist() for _ in range(c["prompts"])]
+
+
+# ---------------------------------------------------------------------------
+# Gate sweep: GATE_SWEEP_BATCHES x GATE_SWEEP_BATCH leaves from seeds, to measure
+# the kernel's residual mismatch against the reference's own gate arithmetic.
+# A batch shares what one gate launch shares (vocabulary, temperature, active
+# count, step); leaves differ in scale, offset, shape, history and EMA.  Every
+# eighth leaf is tie-heavy (logits on a coarse grid, so many exactly equal
+# log-probs) and every eighth + 1 is peaked (a few logits far above the rest).
+# ---------------------------------------------------------------------------
+GATE_SWEEP_BATCH = 256
+GATE_SWEEP_BATCHES = 40
+
+
+def gate_sweep_batch(b):
+    rng = np.random.default_rng(900_000 + b)
+    V = (151936, 128256)[b % 2]
+    T = (0.7, 0.7, 1.0, 0.5)[b % 4]
+    leaves = []
+    for j in range(GATE_SWEEP_BATCH):
+        kind = "ties" if j % 8 == 0 else ("peaked" if j % 8 == 1 else "normal")
+        leaves.append(dict(kind=kind, seed=int(rng.integers(1 << 31)),
+                           scale=float(np.exp(rng.uniform(np.log(0.02), np.log(8.0)))),
+                           offset=float(rng.uniform(-3, 3)), hist=int(rng.integers(0, 300)),
+                           ema_old=None if rng.random() < 0.2 else float(rng.uniform(1.0, 12.0))))
+    return dict(V=V, T=T, penalty=1.2, K=3, M=10, alpha=0.3, mult=1.25, window=10, initial=0.3,
+                num_active=int(rng.integers(1, 11)), step=int(rng.integers(0, 20)), leaves=leaves)
+
+
+def gate_sweep_leaf(batch, leaf):
+    """(bf16-valued float32 logits, generated-token history) of one sweep leaf."""
+    V = batch["V"]
+    rng = np.random.default_rng(leaf["seed"])
+    x = rng.standard_normal(V, dtype=np.float32)
+    if leaf["kind"] == "ties":
+        q = float((2, 4, 8)[leaf["seed"] % 3])
+        x = np.round(x * q) / np.float32(q)
+    x = x * np.float32(leaf["scale"]) + np.float32(leaf["offset"])
+    if leaf["kind"] == "peaked":
+        spikes = rng.integers(0, V, 1 + leaf["seed"] % 4)
+        x[spikes] += rng.uniform(8.0, 30.0, spikes.size).astype(np.float32)
+    hist = rng.integers(0, V, leaf["hist"]).tolist()
+    return bf16_round(x.astype(np.float32)), hist

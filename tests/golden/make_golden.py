@@ -182,6 +182,47 @@ def make_gate():
     print("gate cases", len(res))
 
 
+def make_gate_sweep():
+    """The reference's gate outputs for every leaf of the sweep (tests/golden/cases.py),
+    computed with its own functions on CPU (one thread, as for make_gate)."""
+    from tests.golden.cases import GATE_SWEEP_BATCHES, GATE_SWEEP_BATCH, gate_sweep_batch, gate_sweep_leaf
+    torch.set_num_threads(1)
+    n = GATE_SWEEP_BATCHES * GATE_SWEEP_BATCH
+    out = {k: np.zeros(n, np.float64) for k in ("entropy", "pen_entropy", "ema", "tau")}
+    out.update(branch=np.zeros(n, np.bool_), argmax=np.zeros(n, np.int32), argmax_lp=np.zeros(n, np.float32),
+               topk_ids=np.zeros((n, 3), np.int32), topk_lps=np.zeros((n, 3), np.float32),
+               topk_ties=np.zeros((n, 3), np.int32))
+    gen_self = SimpleNamespace(soft_explore_window=None, soft_explore_initial=None)
+    i = 0
+    for b in range(GATE_SWEEP_BATCHES):
+        c = gate_sweep_batch(b)
+        gen_self.soft_explore_window, gen_self.soft_explore_initial = c["window"], c["initial"]
+        dyn = gu.adaptive_threshold(c["mult"], c["M"], c["num_active"])
+        warm = MentatGenerator._soft_explore_factor(gen_self, c["step"])
+        for leaf in c["leaves"]:
+            x32, hist = gate_sweep_leaf(c, leaf)
+            x = torch.from_numpy(x32).to(torch.bfloat16)
+            H = gu.compute_entropy(x, c["T"])
+            pen = gu.apply_repetition_penalty(x, hist, penalty=c["penalty"])
+            lp = F.log_softmax(pen, dim=-1)
+            am = int(torch.argmax(lp).item())
+            tv, ti = torch.topk(lp, c["K"])
+            eo = leaf["ema_old"]
+            ema = H if eo is None else (c["alpha"] * H) + ((1.0 - c["alpha"]) * eo)
+            tau = ema * dyn * warm
+            out["entropy"][i], out["ema"][i], out["tau"][i] = H, ema, tau
+            out["branch"][i] = (H > tau) and ((c["M"] - c["num_active"]) >= c["K"])
+            out["argmax"][i], out["argmax_lp"][i] = am, float(lp[am].item())
+            out["topk_ids"][i], out["topk_lps"][i] = ti.numpy(), tv.float().numpy()
+            # how many log-probs of the whole vocabulary equal each top-K value: the
+            # order of equal values is implementation-defined in torch.topk
+            out["topk_ties"][i] = [int((lp == v).sum()) for v in tv]
+            out["pen_entropy"][i] = gu.compute_entropy(pen)
+            i += 1
+        print("gate sweep batch", b, flush=True)
+    np.savez_compressed(HERE / "gate_sweep.npz", **out)
+
+
 class _StubTokenizer:
     """The generator's tokenizer interface over space-separated token ids."""
 
@@ -219,7 +260,6 @@ def make_rollout():
 
 
 if __name__ == "__main__":
-    make_alloc_streams()
-    make_attention()
-    make_gate()
-    make_rollout()
+    parts = sys.argv[1:] or ["alloc", "attention", "gate", "rollout", "gate_sweep"]
+    for part in parts:
+        globals()[f"make_{part}" if part != "alloc" else "make_alloc_streams"]()

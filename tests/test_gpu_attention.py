@@ -130,3 +130,56 @@ def test_materialize_matches_oracle_packing():
     k, v, cu, mx = m.build_packed_kv(leaves, 0)
     pk = k.materialize()
     assert pk.shape == k.shape and pk.dtype == k.dtype
+
+
+def test_one_launch_of_1000_branches():
+    """A 1,000-branch tree decodes in one launch (the per-launch limit is 1,024
+    sequences), so the shared prefix is read once for all of them; sampled
+    branches match the fp64 oracle and decoding a branch alone gives its row."""
+    from mentat_b200 import _lib
+    from mentat_b200.attention_backend import attn_decode
+    m, kids, q = c4_like(1000, 512, 1, 40, seed=21)
+    k, v, cu, mx = m.build_packed_kv(kids, 0)
+    n0 = _lib.load().mentat_kernel_launch_count()
+    o = attn_decode(q, k, v, None, cu, mx, len(kids))
+    assert _lib.load().mentat_kernel_launch_count() - n0 <= 5  # lcp, plan, two unit kernels, merge
+    m.check()
+    for i in (0, 511, 999):
+        np.testing.assert_allclose(o[i].float().cpu().numpy(), _oracle_one(m, kids[i], q[i]), atol=2e-3, rtol=1e-2)
+        k1, v1, cu1, mx1 = m.build_packed_kv([kids[i]], 0)
+        torch.testing.assert_close(o[i:i + 1].float(), attn_decode(q[i:i + 1], k1, v1, None, cu1, mx1, 1).float(),
+                                   atol=2e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_plan_reuse_across_layers(dtype):
+    """Layers share the tree's sharing structure, so layer 1 may decode with the
+    plan layer 0 left in the workspace: the result is bit-identical to planning
+    layer 1 itself.  A workspace planned for another batch size is refused on the
+    device (zero output, plan error)."""
+    from mentat_b200 import PagedKVCacheManager, ops
+    g = torch.Generator(device="cuda").manual_seed(5)
+    L, hkv, hq, d = 2, 8, 32, 128
+    m = PagedKVCacheManager(L, hkv, d, max_blocks=2048, block_size=16, device="cuda", dtype=dtype, max_seqs=64)
+    kv = lambda n: torch.randn((n, hkv, d), generator=g, device="cuda").to(dtype)  # noqa: E731
+    root = m.allocate_sequence()
+    for layer in range(L):
+        m.append_tokens(root, layer, kv(700), kv(700))
+    kids = [m.fork_sequence(root) for _ in range(24)]
+    m.free_sequence(root)
+    for i, kid in enumerate(kids):
+        for layer in range(L):
+            m.append_tokens(kid, layer, kv(5 + 7 * i), kv(5 + 7 * i))
+    slots = m._slots_dev(kids)
+    q = torch.randn((len(kids), hq, d), generator=g, device="cuda").to(dtype)
+    mx = max(m.get_kv_length(s) for s in kids)
+    own1 = ops.paged_decode(q, slots, mx, m._op_id, 1, 0.088)
+    ops.paged_decode(q, slots, mx, m._op_id, 0, 0.088)
+    reused = ops.paged_decode(q, slots, mx, m._op_id, 1, 0.088, reuse_plan=True)
+    m.check()
+    assert torch.equal(own1, reused)
+    few = ops.paged_decode(q[:10], slots[:10], mx, m._op_id, 1, 0.088, reuse_plan=True)  # planned for 24
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="plan workspace overflow"):
+        m.check()
+    assert torch.count_nonzero(few).item() == 0
