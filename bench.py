@@ -466,6 +466,18 @@ def run_profile_kernels(args):
     ms = e0.elapsed_time(e1) / steps
     ub = 1024 * 8 * 128 * 2 * 4  # 512 + 8 x 64 distinct tokens
     print(f"config 1 (fp32): {ms * 1e3:.1f} us/call, {ub / ms / 1e6:.1f} GB/s unique KV", flush=True)
+    # PagedKV.materialize (k_gather): the reference's packed K of config 1 (4,608 rows of 4 KB)
+    for _ in range(args.warmup):
+        k1.materialize()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        k1.materialize()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    gb = 4 * 4608 * 8 * 128 * 4  # K and V rows, each read once and written once
+    print(f"gather (materialize): {ms * 1e3:.1f} us/call, {gb / ms / 1e6:.1f} GB/s moved", flush=True)
     m1.check()
 
 
@@ -661,9 +673,13 @@ def run_mentat(args):
     main = torch.cuda.current_stream(device)
     side = torch.cuda.Stream(device)
     x_dev = [torch.empty(nq + 2 * nkv, dtype=torch.bfloat16, device=device) for _ in range(2)]
-    ev_in = [torch.cuda.Event() for _ in range(2)]    # slot filled
-    ev_free = [torch.cuda.Event() for _ in range(2)]  # slot read by its step's kernels
-    ev_out = torch.cuda.Event()
+    # outputs go back from two fixed device slots (a tensor the caching allocator hands
+    # out on one stream and frees while another still reads it stalls the host at times)
+    o_dev = [torch.empty((NBR, HQ, D), dtype=torch.bfloat16, device=device) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # input slot filled
+    ev_free = [torch.cuda.Event() for _ in range(2)]  # input slot read by its step's kernels
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # output slot written
+    ev_back = [torch.cuda.Event() for _ in range(2)]  # output slot copied to the host
 
     def upload(i):
         s = i % 2
@@ -684,11 +700,14 @@ def run_mentat(args):
         ev_free[s].record(main)
         if i + 2 <= last:
             upload(i + 2)
-        ev_out.record(main)
-        side.wait_event(ev_out)
-        o.record_stream(side)
+        if i >= 2:
+            main.wait_event(ev_back[s])
+        o_dev[s].copy_(o, non_blocking=True)
+        ev_out[s].record(main)
+        side.wait_event(ev_out[s])
         with torch.cuda.stream(side):
-            out_host[i].copy_(o, non_blocking=True)
+            out_host[i].copy_(o_dev[s], non_blocking=True)
+            ev_back[s].record(side)
 
     upload(0)
     upload(1)

@@ -587,7 +587,7 @@ class TreeRollout:
             self.steps += 1
             self.step_leaves.append(len(leaves))
             if self.trace is not None:
-                self.trace.append([sorted(lf.seq for lf in lv) for lv in per_tree])
+                self.trace.append([sorted(list(lf.seq) for lf in lv) for lv in per_tree])  # copies: leaves grow
             tokens = torch.tensor([lf.token_ids[-1] for lf in leaves], dtype=torch.long).to(self.device,
                                                                                               non_blocking=True)
             logits, hidden = self.lm.decode(tokens, [lf.seq_id for lf in leaves])
