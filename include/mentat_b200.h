@@ -165,6 +165,26 @@ int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, cons
                                    void* out, int64_t out_stride, float scale, void* workspace,
                                    int64_t workspace_bytes, int32_t max_parts, cudaStream_t s);
 
+/*
+ * Causal prefill attention over the paged cache.  Replaces attn_prefill
+ * (attention_backend.py:175-189 -> flash_attn_func(causal=True) or
+ * _sdpa_prefill :43-96) for one sequence whose K/V the caller has already
+ * appended: query i (i < n) sits at position pos0 + i of the sequence in
+ * slot[0] (device int32[1]) and attends to its positions 0 .. pos0 + i.
+ * pos0 = 0 is a whole-prompt prefill, pos0 > 0 a chunk of a longer one.
+ * q / out: [n][num_q_heads][head_dim] as in mentat_paged_decode.
+ * workspace: mentat_decode_workspace_bytes(n, num_q_heads, head_dim,
+ * max_parts) bytes with max_parts >= mentat_prefill_max_parts(n, pos0).
+ * bf16 / fp16 caches with block_size 16 run on the tensor cores; fp32 on FFMA.
+ * A plan that outgrows max_parts zeroes the output and records
+ * MENTAT_DEV_PLAN_OVERFLOW.  Sliding windows are not supported.
+ */
+int32_t mentat_prefill_max_parts(int32_t n, int32_t pos0);
+int mentat_paged_prefill(const mentat_kv_cache* c, int32_t layer, const int32_t* slot, int32_t n,
+                         int32_t pos0, const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
+                         int64_t out_stride, float scale, void* workspace, int64_t workspace_bytes,
+                         int32_t max_parts, cudaStream_t s);
+
 /* Decode for callers that cannot allocate device memory when they call.
  * No counterpart in the reference.  Some hosts cannot hand this library a
  * workspace: a program that binds the C ABI directly has no caching allocator,

@@ -525,6 +525,75 @@ __global__ void k_plan_reuse(mentat_kv_cache c, int n, int max_parts, int route,
 }
 
 // ---------------------------------------------------------------------------
+// 1c. the plan of a causal prefill: n new queries of one sequence, query i at
+//     position pos0 + i (its tokens 0 .. pos0 + i are cached).  Queries are cut
+//     into row groups of spu positions (the unit kernel's rows / G) and each
+//     group's visible tokens [0, pos0 + last position + 1) into chunks of
+//     prefill_chunk(pos0 + n) tokens; a unit is (group, chunk), with the chunk
+//     number as its partial ordinal.  Groups are written last to first, so the
+//     longest units come first in the queue.
+// ---------------------------------------------------------------------------
+// 512-token chunks give a 2,048-token prompt about 2.5 units per SM on the
+// tensor-core path; longer contexts take longer chunks, so that a query has at
+// most about 16 partials to store and merge (workspace n x parts x Hq x D floats)
+__host__ __device__ inline int prefill_chunk(int64_t len) {
+    const int64_t c = ((len + 15) / 16 + 127) / 128 * 128;
+    return (int)(c < 512 ? 512 : (c > CHUNK_TC ? CHUNK_TC : c));
+}
+
+__global__ void __launch_bounds__(1024)
+k_prefill_plan(mentat_kv_cache c, int n, int pos0, int G, int kind, DecodeWs ws, int max_parts) {
+    __shared__ int smem32[32];
+    __shared__ int s_err;
+    griddep_wait();
+    griddep_launch();
+    const int tid = threadIdx.x;
+    const int spu = max(1, (kind == KIND_TC ? TC_MAX_ROWS : MAX_ROWS) / G);
+    const int chunk = prefill_chunk((int64_t)pos0 + n);
+    const int ngroups = (n + spu - 1) / spu;
+    int32_t* units = kind == KIND_TC ? ws.units_tc : ws.units;
+    if (tid == 0) s_err = 0;
+    int carry = 0;
+    for (int g0 = 0; g0 < ngroups; g0 += blockDim.x) {
+        const int k = g0 + tid;
+        const int g = ngroups - 1 - k;  // last group first
+        int cnt = 0, a = 0, b = 0;
+        if (k < ngroups) {
+            a = g * spu;
+            b = min(n, a + spu);
+            cnt = (pos0 + b + chunk - 1) / chunk;
+            if (cnt > max_parts) atomicExch(&s_err, 1);
+        }
+        int tot;
+        const int base = carry + block_exclusive_scan(cnt, &tot, smem32);
+        if (k < ngroups && base + cnt <= n * max_parts) {
+            for (int ch = 0; ch < cnt && ch < max_parts; ++ch) {
+                int32_t* U = units + (int64_t)(base + ch) * UNIT_INTS;
+                U[0] = a;
+                U[1] = b - 1;
+                U[2] = ch * chunk;
+                U[3] = min((ch + 1) * chunk, pos0 + b);
+                U[4] = ch;
+            }
+            for (int i = a; i < b; ++i) ws.nparts[i] = min(cnt, max_parts);
+        }
+        carry += tot;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const bool err = s_err || carry > n * max_parts;
+        ws.hdr[HDR_NSIMT] = (!err && kind == KIND_FFMA) ? carry : 0;
+        ws.hdr[HDR_NTC] = (!err && kind == KIND_TC) ? carry : 0;
+        ws.hdr[HDR_NTCN] = 0;
+        ws.hdr[HDR_SIMT_NEXT] = ws.hdr[HDR_TC_NEXT] = ws.hdr[HDR_TCN_NEXT] = 0;
+        ws.hdr[HDR_TC_ABORT] = 0;
+        ws.hdr[HDR_ERR] = err ? 1 : 0;
+        ws.hdr[HDR_PLAN_N] = -1;  // not a decode plan: a reuse is refused
+        if (err) set_error(c, MENTAT_DEV_PLAN_OVERFLOW, carry);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // 2. units (FFMA path: any dtype, <= 16 query rows per unit)
 // ---------------------------------------------------------------------------
 constexpr int TT = 32;  // tokens per tile
@@ -533,7 +602,7 @@ constexpr int UNIT_THREADS = 128;
 template <typename T, int D>
 __global__ void __launch_bounds__(UNIT_THREADS)
 k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict__ q, int64_t q_stride, int Hq,
-        float qscale, DecodeWs ws, int max_parts) {
+        float qscale, DecodeWs ws, int max_parts, int causal_pos0) {
     constexpr int TS = UNIT_THREADS / D;  // token splits in the PV stage
     constexpr int KP = D + 1;             // padded K row (conflict-free column reads)
     __shared__ float q_s[MAX_ROWS][D];
@@ -561,7 +630,9 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
         const int32_t* U = ws.units + (int64_t)u * UNIT_INTS;
         const int q_lo = U[0], q_hi = U[1], t0u = U[2], t1u = U[3], ord = U[4];
         const int R = (q_hi - q_lo + 1) * G;
-        const int32_t* tab = table_row(c, layer, slots[q_lo]);
+        // prefill (causal_pos0 >= 0): every row reads the one sequence in slots[0], and
+        // the row of query i sees tokens up to causal_pos0 + i
+        const int32_t* tab = table_row(c, layer, slots[causal_pos0 >= 0 ? 0 : q_lo]);
         for (int idx = tid; idx < R * D; idx += UNIT_THREADS) {
             const int r = idx / D, d = idx % D;
             const int seq = q_lo + r / G, g = r % G;
@@ -617,7 +688,8 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
                 const int j = lane;
                 for (int r = warp; r < R; r += UNIT_THREADS / 32) {
                     float s = -INFINITY;
-                    if (j < cnt) {  // four independent partial sums over the head dimension
+                    const bool seen = j < cnt && (causal_pos0 < 0 || t0 + j <= causal_pos0 + q_lo + r / G);
+                    if (seen) {  // four independent partial sums over the head dimension
                         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 8
                         for (int d = 0; d < D; d += 4) {
@@ -633,14 +705,15 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
                     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
                     const float m_old = m_s[r];
                     const float m_new = fmaxf(m_old, mx);
-                    const float p = (j < cnt) ? exp2f(s - m_new) : 0.f;
+                    // a row with no token seen yet keeps m = -inf and gets p = 0
+                    const float p = (seen && m_new != -INFINITY) ? exp2f(s - m_new) : 0.f;
                     float sum = p;
 #pragma unroll
                     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
                     p_s[r][j] = p;
                     __syncwarp();
                     if (lane == 0) {
-                        const float alpha = exp2f(m_old - m_new);
+                        const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_old - m_new);
                         a_s[r] = alpha;
                         l_s[r] = l_s[r] * alpha + sum;
                         m_s[r] = m_new;
@@ -895,7 +968,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     // tc_min_rows <= G no unit can land in the FFMA queue
     if (!(tc_ok && tc_min_rows() <= G)) {
         if (launch(pdl, k_units<T, D>, dim3(num_sms() * 4), dim3(UNIT_THREADS), 0, s, *c, layer, slots, qt, q_stride,
-                   Hq, qscale, ws, max_parts) != cudaSuccess)
+                   Hq, qscale, ws, max_parts, -1) != cudaSuccess)
             return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
     }
@@ -903,7 +976,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     if constexpr (!std::is_same<T, float>::value) {
         if (tc_ok) {
             if (launch(pdl, k_units_tc<T, D>, dim3(num_sms()), dim3(TC_THREADS), TC_SMEM, s, maps->mk, maps->mv, *c,
-                       layer, slots, qt, q_stride, Hq, qscale, ws, max_parts) != cudaSuccess)
+                       layer, slots, qt, q_stride, Hq, qscale, ws, max_parts, -1) != cudaSuccess)
                 return MENTAT_ERR_CUDA;
             MENTAT_CHECK_LAUNCH();
         }
@@ -924,6 +997,60 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     MENTAT_CHECK_LAUNCH();
     prof_mark(5, s);
     if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;
+    return MENTAT_OK;
+}
+
+// Causal prefill attention of n queries of the sequence in slots[0] (query i at
+// position pos0 + i, its K/V already cached): k_prefill_plan, then the wide
+// tensor-core kernel (bf16 / fp16 caches) or the FFMA kernel (fp32), then the merge.
+template <typename T, int D>
+static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* slot, int n, int pos0, const void* q,
+                          int64_t q_stride, int Hq, void* out, int64_t out_stride, float scale, DecodeWs ws,
+                          int max_parts, cudaStream_t s) {
+    const int G = Hq / c->num_kv_heads;
+    bool tc_ok = false;
+    const PoolMaps* maps = nullptr;
+    if constexpr (!std::is_same<T, float>::value) {
+        tc_ok = tc_supported(c) && ((uintptr_t)q % 16 == 0) && (q_stride % 8 == 0);
+        if (tc_ok) {
+            maps = pool_maps(c, layer);
+            tc_ok = maps != nullptr;
+        }
+        static bool attr[64] = {};
+        int dev = 0;
+        if (tc_ok && (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)) return MENTAT_ERR_CUDA;
+        if (tc_ok && !attr[dev]) {
+            if (cudaFuncSetAttribute(k_units_tc<T, D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
+                cudaSuccess)
+                return MENTAT_ERR_CUDA;
+            attr[dev] = true;
+        }
+    }
+    const bool pdl = pdl_enabled();
+    const int kind = tc_ok ? KIND_TC : KIND_FFMA;
+    if (launch(pdl, k_prefill_plan, dim3(1), dim3(1024), 0, s, *c, n, pos0, G, kind, ws, max_parts) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
+    MENTAT_CHECK_LAUNCH();
+    const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
+    const T* qt = reinterpret_cast<const T*>(q);
+    if (!tc_ok) {
+        if (launch(pdl, k_units<T, D>, dim3(num_sms() * 4), dim3(UNIT_THREADS), 0, s, *c, layer, slot, qt, q_stride,
+                   Hq, qscale, ws, max_parts, pos0) != cudaSuccess)
+            return MENTAT_ERR_CUDA;
+        MENTAT_CHECK_LAUNCH();
+    }
+    if constexpr (!std::is_same<T, float>::value) {
+        if (tc_ok) {
+            if (launch(pdl, k_units_tc<T, D, true>, dim3(num_sms()), dim3(TC_THREADS), TC_SMEM, s, maps->mk, maps->mv, *c,
+                       layer, slot, qt, q_stride, Hq, qscale, ws, max_parts, pos0) != cudaSuccess)
+                return MENTAT_ERR_CUDA;
+            MENTAT_CHECK_LAUNCH();
+        }
+    }
+    if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
+               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride) != cudaSuccess)
+        return MENTAT_ERR_CUDA;
+    MENTAT_CHECK_LAUNCH();
     return MENTAT_OK;
 }
 
@@ -1019,6 +1146,44 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
                         int64_t ws_bytes, int32_t max_parts, cudaStream_t s) {
     return paged_decode(c, layer, slots, n, q, q_stride, Hq, out, out_stride, scale, workspace, ws_bytes,
                         max_parts, false, s);
+}
+
+int32_t mentat_prefill_max_parts(int32_t n, int32_t pos0) {
+    const int64_t len = (int64_t)pos0 + n;
+    const int ch = prefill_chunk(len);
+    return (int32_t)((len + ch - 1) / ch);
+}
+
+int mentat_paged_prefill(const mentat_kv_cache* c, int32_t layer, const int32_t* slot, int32_t n, int32_t pos0,
+                         const void* q, int64_t q_stride, int32_t Hq, void* out, int64_t out_stride, float scale,
+                         void* workspace, int64_t ws_bytes, int32_t max_parts, cudaStream_t s) {
+    if (!c || layer < 0 || layer >= c->num_layers || n < 0 || pos0 < 0 || !c->k_pool || !c->v_pool || Hq <= 0 ||
+        c->num_kv_heads <= 0 || Hq % c->num_kv_heads)
+        return MENTAT_ERR_ARG;
+    if (n == 0) return MENTAT_OK;
+    if (!slot || !q || !out || !workspace || max_parts <= 0) return MENTAT_ERR_ARG;
+    const int G = Hq / c->num_kv_heads;
+    if (G > MAX_ROWS) return MENTAT_ERR_UNSUPPORTED;
+    DecodeWs w;
+    int64_t need = 0;
+    ws_carve(workspace, n, Hq, c->head_dim, max_parts, &w, &need);
+    if (ws_bytes < need) return MENTAT_ERR_ARG;
+    const int D = c->head_dim;
+#define MENTAT_DISPATCH(T)                                                                                       \
+    if (D == 128)                                                                                                \
+        return launch_prefill<T, 128>(c, layer, slot, n, pos0, q, q_stride, Hq, out, out_stride, scale, w,       \
+                                      max_parts, s);                                                             \
+    if (D == 64)                                                                                                 \
+        return launch_prefill<T, 64>(c, layer, slot, n, pos0, q, q_stride, Hq, out, out_stride, scale, w,        \
+                                     max_parts, s);                                                              \
+    return MENTAT_ERR_UNSUPPORTED;
+    switch (c->dtype) {
+        case MENTAT_F32: { MENTAT_DISPATCH(float) }
+        case MENTAT_BF16: { MENTAT_DISPATCH(__nv_bfloat16) }
+        case MENTAT_F16: { MENTAT_DISPATCH(__half) }
+        default: return MENTAT_ERR_UNSUPPORTED;
+    }
+#undef MENTAT_DISPATCH
 }
 
 int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, const int32_t* slots, int32_t n,

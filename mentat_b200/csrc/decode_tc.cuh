@@ -354,11 +354,16 @@ template <> struct Pair<__half> {
 // Roles: warps 0-3 softmax row tile 0, warps 4-7 softmax row tile 1 (TMEM
 // lane quarter = warp % 4), warp 8 lane 0 issues the MMAs, warp 9 the TMA
 // loads (lanes 0-7, one 16-token block each).
-template <typename T, int D>
+// PSPLIT (prefill): P goes to the tensor cores as two 16-bit terms, P_hi =
+// round(P) and P_lo = round(P - P_hi), in TMEM columns 0-63 and 64-127 of the S
+// region, and O takes both products.  A row that sees a few tokens (the first
+// queries of a prompt) would otherwise carry the 2^-9 relative rounding of its
+// one or two weights straight into its output.
+template <typename T, int D, bool PSPLIT = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
            mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict__ q, int64_t q_stride, int Hq,
-           float scale_log2, DecodeWs ws, int max_parts) {
+           float scale_log2, DecodeWs ws, int max_parts, int causal_pos0) {
     constexpr int HALVES = D / 64;                // 128-byte column halves of a row
     constexpr int FMT = Elem<T>::code == MENTAT_BF16 ? 1 : 0;
     constexpr uint32_t IDESC_QK = idesc_f16(FMT, 128, TC_TILE, 0, 0);
@@ -439,7 +444,8 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         const int q_lo = U[0], q_hi = U[1], t0u = U[2], t1u = U[3], ord = U[4];
         const int R = (q_hi - q_lo + 1) * G;
         const int nrt = (R + 127) / 128;
-        const int32_t* tab = table_row(c, layer, slots[q_lo]);
+        // prefill (causal_pos0 >= 0): every row reads the one sequence in slots[0]
+        const int32_t* tab = table_row(c, layer, slots[causal_pos0 >= 0 ? 0 : q_lo]);
         const int blk0 = t0u / 16, blk_end = (t1u + 15) / 16;
         const int nblk = blk_end - blk0;  // <= MAX_BLK
         const int ntiles = (nblk + BPT - 1) / BPT;
@@ -564,6 +570,11 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 umma_f16_ts(od, pa, vd, IDESC_PV, i > 0);
 #pragma unroll
                 for (int k = 1; k < TC_TILE / 16; ++k) umma_ts<true>(od, pa + k * 8, vd + (uint64_t)(k * 2048 / 16), IDESC_PV);
+                if constexpr (PSPLIT) {
+#pragma unroll
+                    for (int k = 0; k < TC_TILE / 16; ++k)
+                        umma_ts<true>(od, pa + 64 + k * 8, vd + (uint64_t)(k * 2048 / 16), IDESC_PV);
+                }
                 if (i == ntiles - 1) umma_commit(bar_o0 + 8 * rt);
                 if (rt == nrt - 1) umma_commit(bar_vempty0 + 8 * vs);
             };
@@ -603,10 +614,12 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
             TC_TRACE(65 + 8 * i);
             if (rows_live) {
                 const int tb = (blk0 + BPT * i) * 16;  // first token of the tile
-                const bool full = tb >= t0u && tb + TC_TILE <= t1u;
+                // prefill: the row of query q_lo + r / G sees tokens up to causal_pos0 + that
+                const int rp = causal_pos0 >= 0 ? causal_pos0 + q_lo + row / G : INT_MAX;
+                const bool full = tb >= t0u && tb + TC_TILE <= t1u && tb + TC_TILE - 1 <= rp;
                 // the row max is taken on raw scores (scale > 0 keeps the order) and the
                 // scale is folded into the exponent's argument: p = 2^(s*scale - m_ref)
-                auto valid = [&](int j) { return full || (tb + j >= t0u && tb + j < t1u); };
+                auto valid = [&](int j) { return full || (tb + j >= t0u && tb + j < t1u && tb + j <= rp); };
                 // tokens 64-127 stay in registers; tokens 0-63 are read for the max
                 // here and again, 32 at a time, for their probabilities
                 float hi[64];
@@ -633,7 +646,8 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     }
                     m_ref = m_new;
                 }
-                const float neg_m = -m_ref;
+                // a row that has seen no token yet (prefill) keeps m = -inf and gets p = 0
+                const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
                 // rows whose reference max rose rescale O; S(i) being complete means
                 // P V(i-1) of this row tile is complete too (issued before S(i))
                 if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
@@ -655,7 +669,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 for (int cchunk = 0; cchunk < 2; ++cchunk) {
                     float v[32];
                     tmem_ld32(s_col + 32 * cchunk, v);
-                    uint32_t pk[16];
+                    uint32_t pk[16], pl[PSPLIT ? 16 : 1];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const int j = 32 * cchunk + 2 * e;
@@ -663,20 +677,24 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                         const float b = valid(j + 1) ? ex2_approx(fmaf(v[2 * e + 1], scale_log2, neg_m)) : 0.f;
                         accs[e & 3] += a + b;
                         pk[e] = Pair<T>::pack(a, b);
+                        if constexpr (PSPLIT) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
                     }
                     tmem_st16(s_col + 16 * cchunk, pk);
+                    if constexpr (PSPLIT) tmem_st16(s_col + 64 + 16 * cchunk, pl);  // S columns already in hi[]
                 }
 #pragma unroll
                 for (int cchunk = 0; cchunk < 2; ++cchunk) {
-                    uint32_t pk[16];
+                    uint32_t pk[16], pl[PSPLIT ? 16 : 1];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const float a = ex2_approx(fmaf(hi[32 * cchunk + 2 * e], scale_log2, neg_m));
                         const float b = ex2_approx(fmaf(hi[32 * cchunk + 2 * e + 1], scale_log2, neg_m));
                         accs[e & 3] += a + b;
                         pk[e] = Pair<T>::pack(a, b);
+                        if constexpr (PSPLIT) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
                     }
                     tmem_st16(s_col + 32 + 16 * cchunk, pk);
+                    if constexpr (PSPLIT) tmem_st16(s_col + 96 + 16 * cchunk, pl);
                 }
                 tmem_st_wait();
                 l_sum += (accs[0] + accs[1]) + (accs[2] + accs[3]);

@@ -158,3 +158,31 @@ _DT = {torch.bfloat16: _lib.MENTAT_BF16, torch.float16: _lib.MENTAT_F16, torch.f
 
 def default_scale(d: int) -> float:
     return 1.0 / math.sqrt(d)
+
+
+def paged_prefill(descp, layer: int, slot: torch.Tensor, pos0: int, q: torch.Tensor, scale: float,
+                  out: torch.Tensor = None) -> torch.Tensor:
+    """Causal prefill attention of ``q`` (n, Hq, D), query i at position pos0 + i
+    of the sequence in ``slot`` (device int32[1]) of the cache described by
+    ``descp`` (a ``ctypes.byref`` of ``_lib.KVCache``); its K/V must already be
+    cached.  Wraps ``mentat_paged_prefill``, PREFILL_QUERIES_PER_LAUNCH queries
+    per call (the workspace grows with queries x partials); the workspace comes
+    from torch's caching allocator on the current stream."""
+    lib = _lib.load()
+    n, hq, d = q.shape
+    if out is None:
+        out = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    for a in range(0, n, PREFILL_QUERIES_PER_LAUNCH):
+        m = min(n - a, PREFILL_QUERIES_PER_LAUNCH)
+        parts = int(lib.mentat_prefill_max_parts(m, pos0 + a))
+        wsb = int(lib.mentat_decode_workspace_bytes(m, hq, d, parts))
+        ws = torch.empty(wsb, device=q.device, dtype=torch.uint8)
+        _lib.check(lib.mentat_paged_prefill(
+            descp, layer, slot.data_ptr(), m, pos0 + a, q.data_ptr() + a * q.stride(0) * q.element_size(),
+            q.stride(0), hq, out.data_ptr() + a * out.stride(0) * out.element_size(), out.stride(0), scale,
+            ws.data_ptr(), wsb, parts, stream), "mentat_paged_prefill")
+    return out
+
+
+PREFILL_QUERIES_PER_LAUNCH = 2048

@@ -499,6 +499,30 @@ class PagedKVCacheManager:
             self._ws_pinned = True
             self._ws_retired = []
 
+    # ---------------------------------------------------------------- prefill
+    def prefill_attention(self, seq_id: int, layer_idx: int, q: torch.Tensor, scale: float = None) -> torch.Tensor:
+        """Causal attention of the last n tokens of ``seq_id`` in layer ``layer_idx``,
+        whose K/V ``append_tokens`` has already cached: ``q`` (n, Hq, D) are their
+        queries, query i at position num_tokens - n + i.  Returns (n, Hq, D).  The
+        paged form of the reference's prefill attention (``attn_prefill``,
+        ``attention_backend.py:175-189``, over the K/V before they were cached);
+        with n < num_tokens it is a chunk of a longer prompt."""
+        seq = self._sequences[seq_id]
+        n, hq, d = q.shape
+        if d != self.head_dim or hq % self.num_key_value_heads:
+            raise ValueError("q shape does not match the cache geometry")
+        if q.dtype != self.dtype:
+            raise TypeError(f"q dtype {q.dtype} differs from the cache dtype {self.dtype}")
+        pos0 = seq.num_tokens[layer_idx] - n
+        if pos0 < 0:
+            raise ValueError(f"{n} queries but only {seq.num_tokens[layer_idx]} cached tokens")
+        if q.stride(2) != 1 or q.stride(1) != d:
+            q = q.contiguous()
+        out = ops.paged_prefill(self._descp, layer_idx, self._slots_dev([seq_id]), pos0, q,
+                                ops.default_scale(d) if scale is None else scale)
+        self._after()
+        return out
+
     # ----------------------------------------------------------- sliding window
     def trim_to_window(self, seq_id: int, window_size: int) -> None:   # :370-417
         seq = self._sequences[seq_id]

@@ -37,7 +37,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib, ops
-from .attention_backend import attn_decode, attn_prefill
+from .attention_backend import attn_decode
 from .gate import Gate, GateConfig
 from .paged_kv_cache import PagedKVCacheManager
 
@@ -218,8 +218,8 @@ class PagedLM:
             attn = blk.self_attn
             q, k, v = self._qkv(attn, blk.input_layernorm(h), (1, L))
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
-            o = attn_prefill(q, k, v)
             self.cache.append_tokens(seq_id, layer_idx, k[0], v[0])
+            o = self.cache.prefill_attention(seq_id, layer_idx, q[0]).view(1, L, self.hq, self.hd)
             h = h + self._sum(attn.o_proj(o.reshape(1, L, -1)))
             h = h + self._sum(blk.mlp(blk.post_attention_layernorm(h)))
         return self.lm_head(self.norm(h)[0, -1])

@@ -1,4 +1,4 @@
-"""Oracle paged GQA decode attention (test infrastructure only).
+"""Oracle paged GQA decode and causal prefill attention (test infrastructure only).
 
 Restates the reference's CPU decode path: ``build_packed_kv``
 (``core/paged_kv_cache.py:289-368``) gathers every sequence's tokens through its
@@ -63,6 +63,32 @@ def packed_decode(q, packed_k, packed_v, cu_seqlens_k, scale=None):
         a, b = int(cu[i]), int(cu[i + 1])
         out[i] = decode_one(q[i], packed_k[a:b], packed_v[a:b], scale)
     return out
+
+
+def prefill(q: np.ndarray, k: np.ndarray, v: np.ndarray, pos0: int = 0, scale: float | None = None):
+    """Causal prefill attention, the reference's ``_sdpa_prefill``
+    (``adapters/attention_backend.py:43-96``): GQA by expanding kv head ``h`` to
+    query heads ``h*G .. h*G+G-1`` (``:70-79``), scale ``1/sqrt(D)``, causal mask
+    (``is_causal=True``, ``:94``).  Generalised to a chunk: q ``(n, Hq, D)`` are
+    the queries of positions ``pos0 .. pos0+n-1`` and k/v ``(pos0+n, Hkv, D)``
+    the whole sequence; query ``i`` sees keys ``0 .. pos0+i`` (``pos0 = 0`` is
+    the reference's whole-prompt call).  Returns ``(n, Hq, D)`` float64."""
+    n, hq, d = q.shape
+    L, hkv, _ = k.shape
+    assert L == pos0 + n, (L, pos0, n)
+    g = hq // hkv
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    q64 = q.astype(np.float64).reshape(n, hkv, g, d)
+    k64 = k.astype(np.float64)
+    v64 = v.astype(np.float64)
+    s = np.einsum("nhgd,lhd->hgnl", q64, k64) * scale
+    mask = np.arange(L)[None, :] <= (pos0 + np.arange(n))[:, None]
+    s = np.where(mask, s, -np.inf)
+    s -= s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    o = np.einsum("hgnl,lhd->nhgd", p, v64)
+    return o.reshape(n, hq, d)
 
 
 def unique_kv_bytes(tables, lens, block_size, num_kv_heads, head_dim, elem_bytes):

@@ -115,6 +115,29 @@ def build_tree_ops(c):
     return ops
 
 
+# causal prefill (attn_prefill, attention_backend.py:175-189): (dtype, batch,
+# prompt length, Hq, Hkv, D, seed); lengths off and on the 16-token block
+PREFILL_CASES = {
+    "f32_g4_s37": ("f32", 1, 37, 8, 2, 128, 11),
+    "f32_g1_d64_s16": ("f32", 2, 16, 4, 4, 64, 12),
+    "bf16_g8_s300": ("bf16", 1, 300, 8, 1, 128, 13),
+    "bf16_g4_d64_b2_s65": ("bf16", 2, 65, 8, 2, 64, 14),
+    "f16_g2_s1": ("f16", 3, 1, 4, 2, 128, 15),
+    "f16_g8_s129": ("f16", 1, 129, 16, 2, 128, 16),
+}
+
+
+def prefill_inputs(name):
+    """q (B, S, Hq, D), k and v (B, S, Hkv, D), float32, rounded to the case's dtype."""
+    dt, B, S, hq, hkv, d, seed = PREFILL_CASES[name]
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, S, hq, d), dtype=np.float32)
+    k = rng.standard_normal((B, S, hkv, d), dtype=np.float32)
+    v = rng.standard_normal((B, S, hkv, d), dtype=np.float32)
+    rnd = {"f32": lambda a: a, "bf16": bf16_round, "f16": lambda a: a.astype(np.float16).astype(np.float32)}[dt]
+    return tuple(rnd(a) for a in (q, k, v))
+
+
 def attn_inputs(c):
     """q, per-append K/V arrays (float32) and the pool permutation."""
     rng = np.random.default_rng(c["seed"])

@@ -150,6 +150,20 @@ def make_attention():
     print("attention cases", len(ATTN_CASES))
 
 
+def make_prefill():
+    """The reference's attn_prefill (SDPA backend, CPU) on the prefill cases, in
+    the case's dtype; outputs stored as float32."""
+    from tests.golden.cases import PREFILL_CASES, prefill_inputs
+    out = {}
+    for name, c in PREFILL_CASES.items():
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[c[0]]
+        q, k, v = (torch.from_numpy(a).to(dt) for a in prefill_inputs(name))
+        o = ab.attn_prefill(q, k, v)
+        out[f"{name}__out"] = o.float().numpy()
+    np.savez_compressed(HERE / "prefill.npz", **out)
+    print("prefill cases", len(PREFILL_CASES))
+
+
 def make_gate():
     torch.set_num_threads(1)
     gen_self = SimpleNamespace(soft_explore_window=None, soft_explore_initial=None)
@@ -260,6 +274,6 @@ def make_rollout():
 
 
 if __name__ == "__main__":
-    parts = sys.argv[1:] or ["alloc", "attention", "gate", "rollout", "gate_sweep"]
+    parts = sys.argv[1:] or ["alloc", "attention", "prefill", "gate", "rollout", "gate_sweep"]
     for part in parts:
         globals()[f"make_{part}" if part != "alloc" else "make_alloc_streams"]()

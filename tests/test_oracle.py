@@ -7,9 +7,10 @@ import numpy as np
 import pytest
 
 from oracle.allocator import OraclePagedKV
-from oracle.attention import paged_decode, unique_kv_bytes
+from oracle.attention import paged_decode, prefill, unique_kv_bytes
 from oracle.gate import gate_leaf, log_softmax_bf16, apply_penalty, bf16_round
-from tests.golden.cases import ATTN_CASES, attn_inputs, build_tree_ops, gate_inputs
+from tests.golden.cases import (ATTN_CASES, PREFILL_CASES, attn_inputs, build_tree_ops, gate_inputs,
+                                prefill_inputs)
 
 HERE = os.path.dirname(__file__)
 
@@ -157,3 +158,21 @@ def test_oracle_gate_sweep_first_batch():
         miss["branch"] += r["branch"] != bool(g["branch"][i])
     assert miss["entropy"] <= 1 and miss["argmax"] <= 1 and miss["branch"] <= 1, miss
     assert miss["pen_entropy"] <= 3, miss
+
+
+# The reference's CPU SDPA in bf16 / fp16 rounds its probabilities to the input
+# dtype, so its outputs sit up to 8e-3 (bf16) / 1.1e-3 (fp16) from the exact values.
+PREFILL_TOL = {"f32": 1e-5, "bf16": 1e-2, "f16": 2e-3}
+
+
+@pytest.mark.parametrize("name", sorted(PREFILL_CASES))
+def test_oracle_prefill(name):
+    """The causal prefill restatement against the reference's attn_prefill."""
+    g = np.load(os.path.join(HERE, "golden", "prefill.npz"))
+    q, k, v = prefill_inputs(name)
+    o = np.stack([prefill(q[b], k[b], v[b]) for b in range(q.shape[0])])
+    np.testing.assert_allclose(o, g[f"{name}__out"], atol=PREFILL_TOL[PREFILL_CASES[name][0]], rtol=0)
+    # a chunk of queries (pos0 > 0) gives the rows of the whole-prompt call
+    S = q.shape[1]
+    for pos0 in sorted({0, S // 3, S - 1}):
+        np.testing.assert_array_equal(prefill(q[0][pos0:], k[0], v[0], pos0=pos0), o[0][pos0:])
