@@ -481,6 +481,63 @@ def run_profile_kernels(args):
     m1.check()
 
 
+def run_profile_prefill(args):
+    """Causal prefill attention of one prompt per length in --profile-prefill:
+    bf16, Hq 32, Hkv 8, D 128 (the benchmark trees' head geometry).  Times the
+    paged prefill over the cache (PagedKVCacheManager.prefill_attention), the
+    dense drop-in (attn_prefill), and, for comparison, torch's SDPA (flash
+    backend) and flash_attn_func on the same tensors.  FLOPs count the causal
+    half: 4 x Hq x D x S (S + 1) / 2."""
+    import torch.nn.functional as F
+    from mentat_b200 import PagedKVCacheManager
+    from mentat_b200.attention_backend import attn_prefill
+    try:
+        from flash_attn import flash_attn_func
+    except Exception:  # noqa: BLE001 - optional comparison
+        flash_attn_func = None
+    device = torch.device("cuda", 0)
+    steps = max(args.steps, 1)
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    hq, hkv, d = 32, 8, 128
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    for S in (int(x) for x in args.profile_prefill.split(",")):
+        q = torch.randn((1, S, hq, d), generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn((1, S, hkv, d), generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn((1, S, hkv, d), generator=g, device=device).to(torch.bfloat16)
+        m = PagedKVCacheManager(1, hkv, d, max_blocks=(S + 15) // 16 + 2, block_size=16, device=device,
+                                dtype=torch.bfloat16, max_seqs=2)
+        sid = m.allocate_sequence()
+        m.append_tokens(sid, 0, k[0], v[0])
+        flops = 4.0 * hq * d * S * (S + 1) / 2
+        row = {"S": S}
+        row["paged"] = timed(lambda: m.prefill_attention(sid, 0, q[0]))
+        row["dense"] = timed(lambda: attn_prefill(q, k, v))
+        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        row["sdpa"] = timed(lambda: F.scaled_dot_product_attention(qt, kt, vt, is_causal=True, enable_gqa=True))
+        if flash_attn_func is not None:
+            try:
+                row["flash_attn"] = timed(lambda: flash_attn_func(q, k, v, causal=True))
+            except Exception as e:  # noqa: BLE001 - no kernels for this GPU
+                print(f"flash_attn_func unavailable: {str(e).splitlines()[0][:120]}", flush=True)
+        m.check()
+        print("prefill S=%d: " % S + ", ".join(
+            f"{key} {ms * 1e3:.1f} us ({flops / ms / 1e9:.0f} TFLOP/s)" for key, ms in row.items() if key != "S"),
+            flush=True)
+        del m
+
+
 def run_profile_case(args):
     """A smaller tree for a profiler capture: warm-up calls, then --steps decode
     calls of attn_decode; prints the mean time per call (no JSON line)."""
@@ -813,12 +870,17 @@ def main():
                     help="skip the config-3 tree tokens/s measurement of the default run")
     ap.add_argument("--profile-case", default=None, metavar="PREFIX,BRANCHES,SUFFIX",
                     help="time a smaller tree for a profiler capture instead of the benchmark")
+    ap.add_argument("--profile-prefill", default=None, metavar="LEN[,LEN...]",
+                    help="time causal prefill attention of prompts of these lengths (no JSON line)")
     ap.add_argument("--profile-kernels", action="store_true",
                     help="time the gate and append kernels for a profiler capture instead of the benchmark")
     ap.add_argument("--tree-config", type=int, default=None, choices=sorted(TREE_CONFIGS),
                     help="tree tokens/s of the entropy-gated rollout on a benchmark model config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile_prefill:
+        run_profile_prefill(args)
+        return
     if args.profile_case:
         run_profile_case(args)
     elif args.profile_kernels:

@@ -174,12 +174,16 @@ int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, cons
  * pos0 = 0 is a whole-prompt prefill, pos0 > 0 a chunk of a longer one.
  * q / out: [n][num_q_heads][head_dim] as in mentat_paged_decode.
  * workspace: mentat_decode_workspace_bytes(n, num_q_heads, head_dim,
- * max_parts) bytes with max_parts >= mentat_prefill_max_parts(n, pos0).
- * bf16 / fp16 caches with block_size 16 run on the tensor cores; fp32 on FFMA.
- * A plan that outgrows max_parts zeroes the output and records
- * MENTAT_DEV_PLAN_OVERFLOW.  Sliding windows are not supported.
+ * max_parts) bytes with max_parts >= mentat_prefill_max_parts(c, n, pos0,
+ * num_q_heads), the partials a query can have (1 when every query group's
+ * tokens fit one unit; 0 for invalid arguments).
+ * bf16 / fp16 caches with block_size 16 run on the tensor cores (out 16-byte
+ * aligned with out_stride a multiple of 8: single-partial rows are written by
+ * the unit kernel itself); fp32 on FFMA.  A plan that outgrows max_parts zeroes
+ * the output and records MENTAT_DEV_PLAN_OVERFLOW.  Sliding windows are not
+ * supported.
  */
-int32_t mentat_prefill_max_parts(int32_t n, int32_t pos0);
+int32_t mentat_prefill_max_parts(const mentat_kv_cache* c, int32_t n, int32_t pos0, int32_t num_q_heads);
 int mentat_paged_prefill(const mentat_kv_cache* c, int32_t layer, const int32_t* slot, int32_t n,
                          int32_t pos0, const void* q, int64_t q_stride, int32_t num_q_heads, void* out,
                          int64_t out_stride, float scale, void* workspace, int64_t workspace_bytes,

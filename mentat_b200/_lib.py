@@ -76,7 +76,7 @@ SIGNATURES = [
      [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
     ("mentat_paged_decode_noalloc", C.c_int, [_KV, _I32, _P, _I32, _P, _I64, _I32, _P, _I64, _F, _I32, _P]),
     ("mentat_decode_set_wait_probe", C.c_int, [_I64]),
-    ("mentat_prefill_max_parts", _I32, [_I32, _I32]),
+    ("mentat_prefill_max_parts", _I32, [_KV, _I32, _I32, _I32]),
     ("mentat_paged_prefill", C.c_int,
      [_KV, _I32, _P, _I32, _I32, _P, _I64, _I32, _P, _I64, _F, _P, _I64, _I32, _P]),
     ("mentat_profile_enable", C.c_int, [_I32]),

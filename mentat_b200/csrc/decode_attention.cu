@@ -533,23 +533,14 @@ __global__ void k_plan_reuse(mentat_kv_cache c, int n, int max_parts, int route,
 //     number as its partial ordinal.  Groups are written last to first, so the
 //     longest units come first in the queue.
 // ---------------------------------------------------------------------------
-// 512-token chunks give a 2,048-token prompt about 2.5 units per SM on the
-// tensor-core path; longer contexts take longer chunks, so that a query has at
-// most about 16 partials to store and merge (workspace n x parts x Hq x D floats)
-__host__ __device__ inline int prefill_chunk(int64_t len) {
-    const int64_t c = ((len + 15) / 16 + 127) / 128 * 128;
-    return (int)(c < 512 ? 512 : (c > CHUNK_TC ? CHUNK_TC : c));
-}
-
 __global__ void __launch_bounds__(1024)
-k_prefill_plan(mentat_kv_cache c, int n, int pos0, int G, int kind, DecodeWs ws, int max_parts) {
+k_prefill_plan(mentat_kv_cache c, int n, int pos0, int G, int kind, int chunk, DecodeWs ws, int max_parts) {
     __shared__ int smem32[32];
     __shared__ int s_err;
     griddep_wait();
     griddep_launch();
     const int tid = threadIdx.x;
     const int spu = max(1, (kind == KIND_TC ? TC_MAX_ROWS : MAX_ROWS) / G);
-    const int chunk = prefill_chunk((int64_t)pos0 + n);
     const int ngroups = (n + spu - 1) / spu;
     int32_t* units = kind == KIND_TC ? ws.units_tc : ws.units;
     if (tid == 0) s_err = 0;
@@ -768,7 +759,8 @@ constexpr int MERGE_WARPS = 4;  // warps per CTA
 
 template <typename T, int D>
 __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
-                                                          int max_parts, T* __restrict__ out, int64_t out_stride) {
+                                                          int max_parts, T* __restrict__ out, int64_t out_stride,
+                                                          int skip_single) {
     constexpr int WPP = D / 64;  // warps per (sequence, head)
     constexpr int B = 18;        // partial rows in flight per lane (config 4 has 17-18 partials)
     griddep_wait();  // every unit kernel's partials
@@ -795,6 +787,8 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
     // is clamped so that no row past the workspace is read.
     const bool aborted = ws.hdr[HDR_TC_ABORT] != 0 || ws.hdr[HDR_ERR] != 0;
     const int P = aborted ? 0 : min(ws.nparts[i], max_parts);
+    // prefill: the unit kernel wrote the output of a query with one partial itself
+    if (skip_single && P == 1) return;
     if (ws.hdr[HDR_TC_ABORT] != 0 && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
     // (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
     auto comb = [](float& m, float& l, float m2, float l2) {
@@ -976,7 +970,8 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     if constexpr (!std::is_same<T, float>::value) {
         if (tc_ok) {
             if (launch(pdl, k_units_tc<T, D>, dim3(num_sms()), dim3(TC_THREADS), TC_SMEM, s, maps->mk, maps->mv, *c,
-                       layer, slots, qt, q_stride, Hq, qscale, ws, max_parts, -1) != cudaSuccess)
+                       layer, slots, qt, q_stride, Hq, qscale, ws, max_parts, -1, (T*)nullptr, (int64_t)0) !=
+                cudaSuccess)
                 return MENTAT_ERR_CUDA;
             MENTAT_CHECK_LAUNCH();
         }
@@ -992,12 +987,27 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     }
     prof_mark(4, s);
     if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
-               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride) != cudaSuccess)
+               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride, 0) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     prof_mark(5, s);
     if (g_prof_on && g_prof_n < g_prof_cap) ++g_prof_n;
     return MENTAT_OK;
+}
+
+// Chunk length of a prefill's units.  A query group's units run one after
+// another on one SM, so a group may take its whole range in one unit (one
+// partial per query, no merge) when that range is no longer than the average
+// work per SM; otherwise its range is cut into chunks of about that average.
+static int prefill_chunk_for(int n, int pos0, int G, int hkv, int kind) {
+    const int64_t L = (int64_t)pos0 + n;
+    const int spu = std::max(1, (kind == KIND_TC ? TC_MAX_ROWS : MAX_ROWS) / G);
+    const int64_t ngroups = (n + spu - 1) / spu;
+    int64_t total = 0;  // tokens seen by all groups: group g's last query is min(n, (g + 1) spu) - 1
+    for (int64_t g = 0; g < ngroups; ++g) total += pos0 + std::min<int64_t>(n, (g + 1) * spu);
+    const int64_t avg = total * hkv / std::max(1, num_sms());
+    if (L <= avg) return (int)std::min<int64_t>((L + 15) / 16 * 16, INT32_MAX - 15);
+    return (int)((std::max<int64_t>(avg, 256) + 127) / 128 * 128);
 }
 
 // Causal prefill attention of n queries of the sequence in slots[0] (query i at
@@ -1028,7 +1038,11 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
     }
     const bool pdl = pdl_enabled();
     const int kind = tc_ok ? KIND_TC : KIND_FFMA;
-    if (launch(pdl, k_prefill_plan, dim3(1), dim3(1024), 0, s, *c, n, pos0, G, kind, ws, max_parts) != cudaSuccess)
+    const int chunk = prefill_chunk_for(n, pos0, G, c->num_kv_heads, kind);
+    // the tensor-core kernel writes the rows of single-partial queries itself
+    const bool direct = tc_ok && (uintptr_t)out % 16 == 0 && out_stride % 8 == 0;
+    if (launch(pdl, k_prefill_plan, dim3(1), dim3(1024), 0, s, *c, n, pos0, G, kind, chunk, ws, max_parts) !=
+        cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
@@ -1042,13 +1056,14 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
     if constexpr (!std::is_same<T, float>::value) {
         if (tc_ok) {
             if (launch(pdl, k_units_tc<T, D, true>, dim3(num_sms()), dim3(TC_THREADS), TC_SMEM, s, maps->mk, maps->mv, *c,
-                       layer, slot, qt, q_stride, Hq, qscale, ws, max_parts, pos0) != cudaSuccess)
+                       layer, slot, qt, q_stride, Hq, qscale, ws, max_parts, pos0,
+                       direct ? reinterpret_cast<T*>(out) : (T*)nullptr, out_stride) != cudaSuccess)
                 return MENTAT_ERR_CUDA;
             MENTAT_CHECK_LAUNCH();
         }
     }
     if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
-               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride) != cudaSuccess)
+               0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride, direct ? 1 : 0) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
     return MENTAT_OK;
@@ -1148,9 +1163,14 @@ int mentat_paged_decode(const mentat_kv_cache* c, int32_t layer, const int32_t* 
                         max_parts, false, s);
 }
 
-int32_t mentat_prefill_max_parts(int32_t n, int32_t pos0) {
+int32_t mentat_prefill_max_parts(const mentat_kv_cache* c, int32_t n, int32_t pos0, int32_t num_q_heads) {
+    if (!c || n <= 0 || pos0 < 0 || c->num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % c->num_kv_heads)
+        return 0;
+    // with the tensor-core kernel's query groups; the FFMA kernel's groups are
+    // smaller, see more tokens in total and take longer chunks, so no more parts
+    const int kind = tc_supported(c) ? KIND_TC : KIND_FFMA;
     const int64_t len = (int64_t)pos0 + n;
-    const int ch = prefill_chunk(len);
+    const int ch = prefill_chunk_for(n, pos0, num_q_heads / c->num_kv_heads, c->num_kv_heads, kind);
     return (int32_t)((len + ch - 1) / ch);
 }
 

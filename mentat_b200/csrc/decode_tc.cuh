@@ -33,6 +33,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 namespace mentat {
 
 #ifdef MENTAT_TC_TRACE
@@ -354,16 +356,25 @@ template <> struct Pair<__half> {
 // Roles: warps 0-3 softmax row tile 0, warps 4-7 softmax row tile 1 (TMEM
 // lane quarter = warp % 4), warp 8 lane 0 issues the MMAs, warp 9 the TMA
 // loads (lanes 0-7, one 16-token block each).
-// PSPLIT (prefill): P goes to the tensor cores as two 16-bit terms, P_hi =
-// round(P) and P_lo = round(P - P_hi), in TMEM columns 0-63 and 64-127 of the S
-// region, and O takes both products.  A row that sees a few tokens (the first
-// queries of a prompt) would otherwise carry the 2^-9 relative rounding of its
-// one or two weights straight into its output.
-template <typename T, int D, bool PSPLIT = false>
+// PREFILL (the causal prefill instantiation):
+//  * in the sequence's first tile (tokens 0-127), P goes to the tensor cores as
+//    two 16-bit terms, P_hi = round(P) and P_lo = round(P - P_hi), in TMEM
+//    columns 0-63 and 64-127 of the S region, and O takes both products.  The
+//    rows of the first 128 queries see only that tile; one that sees a few
+//    tokens would otherwise carry the 2^-9 relative rounding of its one or two
+//    weights straight into its output.  Later tiles round P once, as decode
+//    (and flash attention) do, where many weights average the rounding out.
+//  * a unit may span any number of tiles: the TMA warp reads each tile's block
+//    ids one tile ahead instead of the whole unit's up front.
+//  * with out != nullptr, the softmax threads of a unit whose queries have one
+//    partial (the unit covers their whole range) write their rows' normalised
+//    outputs straight to out; the merge skips those queries.
+template <typename T, int D, bool PREFILL = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
            mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict__ q, int64_t q_stride, int Hq,
-           float scale_log2, DecodeWs ws, int max_parts, int causal_pos0) {
+           float scale_log2, DecodeWs ws, int max_parts, int causal_pos0, T* __restrict__ out, int64_t out_stride) {
+    constexpr bool PSPLIT = PREFILL;
     constexpr int HALVES = D / 64;                // 128-byte column halves of a row
     constexpr int FMT = Elem<T>::code == MENTAT_BF16 ? 1 : 0;
     constexpr uint32_t IDESC_QK = idesc_f16(FMT, 128, TC_TILE, 0, 0);
@@ -447,21 +458,24 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         // prefill (causal_pos0 >= 0): every row reads the one sequence in slots[0]
         const int32_t* tab = table_row(c, layer, slots[causal_pos0 >= 0 ? 0 : q_lo]);
         const int blk0 = t0u / 16, blk_end = (t1u + 15) / 16;
-        const int nblk = blk_end - blk0;  // <= MAX_BLK
+        const int nblk = blk_end - blk0;  // <= MAX_BLK unless PREFILL
         const int ntiles = (nblk + BPT - 1) / BPT;
 
         // The TMA warp reads the unit's block ids and starts streaming K/V at
         // once; the other warps stage Q meanwhile (all loads in flight together)
         // and meet on named barrier 2 before the first MMA.
         if (tma_warp) {
-            constexpr int PER_LANE = (MAX_BLK + 31) / 32;
-            int b[PER_LANE];
+            if constexpr (!PREFILL) {
+                constexpr int PER_LANE = (MAX_BLK + 31) / 32;
+                int b[PER_LANE];
 #pragma unroll
-            for (int k = 0; k < PER_LANE; ++k) b[k] = lane + 32 * k < nblk ? checked_block(c, tab[blk0 + lane + 32 * k]) : 0;
+                for (int k = 0; k < PER_LANE; ++k)
+                    b[k] = lane + 32 * k < nblk ? checked_block(c, tab[blk0 + lane + 32 * k]) : 0;
 #pragma unroll
-            for (int k = 0; k < PER_LANE; ++k)
-                if (lane + 32 * k < nblk) s_blk[lane + 32 * k] = b[k];
-            __syncwarp();
+                for (int k = 0; k < PER_LANE; ++k)
+                    if (lane + 32 * k < nblk) s_blk[lane + 32 * k] = b[k];
+                __syncwarp();
+            }
         } else {
             constexpr int QCH = 2 * 128 * (D / 8);                  // 16-byte Q chunks of two row tiles
             constexpr int NQ = TC_THREADS - 32;                     // loading threads (TMA warp excluded)
@@ -499,10 +513,19 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
 
         if (tma_warp) {
             // K(i) then V(i); a stage is reused once every row tile's MMA that read it is done
+            int blk_next = 0;  // PREFILL: block ids one tile ahead
+            if constexpr (PREFILL) blk_next = lane < min(BPT, nblk) ? checked_block(c, tab[blk0 + lane]) : 0;
             for (int i = 0; i < ntiles; ++i) {
                 const uint32_t gi = g0 + i, ks = gi % TC_KST, vs = gi % TC_VST;
                 const int nb = min(BPT, nblk - BPT * i);
-                const int blk = lane < nb ? s_blk[BPT * i + lane] : 0;
+                int blk;
+                if constexpr (PREFILL) {
+                    blk = blk_next;
+                    const int nb2 = min(BPT, nblk - BPT * (i + 1));
+                    blk_next = lane < nb2 ? checked_block(c, tab[blk0 + BPT * (i + 1) + lane]) : 0;
+                } else {
+                    blk = lane < nb ? s_blk[BPT * i + lane] : 0;
+                }
                 int ok = 1;
                 if (lane == 0) {
                     if (gi >= TC_KST) ok = mbar_wait(bar_kempty0 + 8 * ks, ((gi / TC_KST) - 1) & 1);
@@ -570,7 +593,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 umma_f16_ts(od, pa, vd, IDESC_PV, i > 0);
 #pragma unroll
                 for (int k = 1; k < TC_TILE / 16; ++k) umma_ts<true>(od, pa + k * 8, vd + (uint64_t)(k * 2048 / 16), IDESC_PV);
-                if constexpr (PSPLIT) {
+                if (PSPLIT && blk0 + BPT * i == 0) {  // P_lo of the sequence's first tile
 #pragma unroll
                     for (int k = 0; k < TC_TILE / 16; ++k)
                         umma_ts<true>(od, pa + 64 + k * 8, vd + (uint64_t)(k * 2048 / 16), IDESC_PV);
@@ -620,84 +643,111 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 // the row max is taken on raw scores (scale > 0 keeps the order) and the
                 // scale is folded into the exponent's argument: p = 2^(s*scale - m_ref)
                 auto valid = [&](int j) { return full || (tb + j >= t0u && tb + j < t1u && tb + j <= rp); };
-                // tokens 64-127 stay in registers; tokens 0-63 are read for the max
-                // here and again, 32 at a time, for their probabilities
-                float hi[64];
-                float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
-                {
-                    float lo[64];
-                    tmem_ld64(s_col, lo);
+                // MASKED: some token of the warp's rows is outside the unit's range or
+                // (prefill) after the row's position; a warp whose rows see the whole
+                // tile runs the copy without the per-score checks
+                auto tile_body = [&](auto masked_c) {
+                    constexpr bool MASKED = decltype(masked_c)::value;
+                    auto ok = [&](int j) {
+                        if constexpr (MASKED) return valid(j);
+                        else return true;
+                    };
+                    // tokens 64-127 stay in registers; tokens 0-63 are read for the max
+                    // here and again, 32 at a time, for their probabilities
+                    float hi[64];
+                    float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
+                    {
+                        float lo[64];
+                        tmem_ld64(s_col, lo);
 #pragma unroll
-                    for (int j = 0; j < 64; ++j) mxs[j & 3] = fmaxf(mxs[j & 3], valid(j) ? lo[j] : -INFINITY);
-                }
-                tmem_ld64(s_col + 64, hi);
-#pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    if (!valid(64 + j)) hi[j] = -INFINITY;
-                    mxs[j & 3] = fmaxf(mxs[j & 3], hi[j]);
-                }
-                const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
-                float fac = 1.f;
-                const float m_new = fmaxf(m_ref, mx * scale_log2);
-                if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
-                    if (m_ref != -INFINITY) {
-                        fac = ex2_approx(m_ref - m_new);
-                        l_sum *= fac;
+                        for (int j = 0; j < 64; ++j) mxs[j & 3] = fmaxf(mxs[j & 3], ok(j) ? lo[j] : -INFINITY);
                     }
-                    m_ref = m_new;
-                }
-                // a row that has seen no token yet (prefill) keeps m = -inf and gets p = 0
-                const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-                // rows whose reference max rose rescale O; S(i) being complete means
-                // P V(i-1) of this row tile is complete too (issued before S(i))
-                if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
-                    const float f = row < R ? fac : 1.f;
+                    tmem_ld64(s_col + 64, hi);
 #pragma unroll
-                    for (int cb = 0; cb < D / 32; ++cb) {
-                        float ov[32];
-                        tmem_ld32(o_col + cb * 32, ov);
-#pragma unroll
-                        for (int k = 0; k < 32; ++k) ov[k] *= f;
-                        tmem_st32(o_col + cb * 32, ov);
+                    for (int j = 0; j < 64; ++j) {
+                        if (!ok(64 + j)) hi[j] = -INFINITY;
+                        mxs[j & 3] = fmaxf(mxs[j & 3], hi[j]);
                     }
-                }
-                // P (pairs packed in one column) over the consumed S columns: the P of
-                // tokens 0-63 lands in columns 0-31, that of tokens 64-127 in 32-63,
-                // each written after the S columns it overwrites have been read
-                float accs[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
-#pragma unroll
-                for (int cchunk = 0; cchunk < 2; ++cchunk) {
-                    float v[32];
-                    tmem_ld32(s_col + 32 * cchunk, v);
-                    uint32_t pk[16], pl[PSPLIT ? 16 : 1];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int j = 32 * cchunk + 2 * e;
-                        const float a = valid(j) ? ex2_approx(fmaf(v[2 * e], scale_log2, neg_m)) : 0.f;
-                        const float b = valid(j + 1) ? ex2_approx(fmaf(v[2 * e + 1], scale_log2, neg_m)) : 0.f;
-                        accs[e & 3] += a + b;
-                        pk[e] = Pair<T>::pack(a, b);
-                        if constexpr (PSPLIT) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
+                    const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+                    float fac = 1.f;
+                    const float m_new = fmaxf(m_ref, mx * scale_log2);
+                    if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
+                        if (m_ref != -INFINITY) {
+                            fac = ex2_approx(m_ref - m_new);
+                            l_sum *= fac;
+                        }
+                        m_ref = m_new;
                     }
-                    tmem_st16(s_col + 16 * cchunk, pk);
-                    if constexpr (PSPLIT) tmem_st16(s_col + 64 + 16 * cchunk, pl);  // S columns already in hi[]
-                }
+                    // a row that has seen no token yet (prefill) keeps m = -inf and gets p = 0
+                    const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+                    // rows whose reference max rose rescale O; S(i) being complete means
+                    // P V(i-1) of this row tile is complete too (issued before S(i))
+                    if (i > 0 && __any_sync(0xffffffffu, fac != 1.f)) {
+                        const float f = row < R ? fac : 1.f;
 #pragma unroll
-                for (int cchunk = 0; cchunk < 2; ++cchunk) {
-                    uint32_t pk[16], pl[PSPLIT ? 16 : 1];
+                        for (int cb = 0; cb < D / 32; ++cb) {
+                            float ov[32];
+                            tmem_ld32(o_col + cb * 32, ov);
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const float a = ex2_approx(fmaf(hi[32 * cchunk + 2 * e], scale_log2, neg_m));
-                        const float b = ex2_approx(fmaf(hi[32 * cchunk + 2 * e + 1], scale_log2, neg_m));
-                        accs[e & 3] += a + b;
-                        pk[e] = Pair<T>::pack(a, b);
-                        if constexpr (PSPLIT) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
+                            for (int k = 0; k < 32; ++k) ov[k] *= f;
+                            tmem_st32(o_col + cb * 32, ov);
+                        }
                     }
-                    tmem_st16(s_col + 32 + 16 * cchunk, pk);
-                    if constexpr (PSPLIT) tmem_st16(s_col + 96 + 16 * cchunk, pl);
-                }
-                tmem_st_wait();
-                l_sum += (accs[0] + accs[1]) + (accs[2] + accs[3]);
+                    // P (pairs packed in one column) over the consumed S columns: the P of
+                    // tokens 0-63 lands in columns 0-31, that of tokens 64-127 in 32-63,
+                    // each written after the S columns it overwrites have been read
+                    float accs[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
+                    // SP: also P_lo (prefill, first tile of the sequence only)
+                    auto write_p = [&](auto sp_c) {
+                        constexpr bool SP = decltype(sp_c)::value;
+#pragma unroll
+                        for (int cchunk = 0; cchunk < 2; ++cchunk) {
+                            float v[32];
+                            tmem_ld32(s_col + 32 * cchunk, v);
+                            uint32_t pk[16], pl[SP ? 16 : 1];
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const int j = 32 * cchunk + 2 * e;
+                                // a masked score enters as -inf: 2^-inf = 0, no branch
+                                const float a = ex2_approx(fmaf(ok(j) ? v[2 * e] : -INFINITY, scale_log2, neg_m));
+                                const float b = ex2_approx(fmaf(ok(j + 1) ? v[2 * e + 1] : -INFINITY, scale_log2, neg_m));
+                                accs[e & 3] += a + b;
+                                pk[e] = Pair<T>::pack(a, b);
+                                if constexpr (SP) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
+                            }
+                            tmem_st16(s_col + 16 * cchunk, pk);
+                            if constexpr (SP) tmem_st16(s_col + 64 + 16 * cchunk, pl);  // S columns already in hi[]
+                        }
+#pragma unroll
+                        for (int cchunk = 0; cchunk < 2; ++cchunk) {
+                            uint32_t pk[16], pl[SP ? 16 : 1];
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const float a = ex2_approx(fmaf(hi[32 * cchunk + 2 * e], scale_log2, neg_m));
+                                const float b = ex2_approx(fmaf(hi[32 * cchunk + 2 * e + 1], scale_log2, neg_m));
+                                accs[e & 3] += a + b;
+                                pk[e] = Pair<T>::pack(a, b);
+                                if constexpr (SP) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
+                            }
+                            tmem_st16(s_col + 32 + 16 * cchunk, pk);
+                            if constexpr (SP) tmem_st16(s_col + 96 + 16 * cchunk, pl);
+                        }
+                    };
+                    if constexpr (PSPLIT) {
+                        if (tb == 0)
+                            write_p(std::true_type{});
+                        else
+                            write_p(std::false_type{});
+                    } else {
+                        write_p(std::false_type{});
+                    }
+                    tmem_st_wait();
+                    l_sum += (accs[0] + accs[1]) + (accs[2] + accs[3]);
+                };
+                if (__all_sync(0xffffffffu, full))
+                    tile_body(std::false_type{});
+                else
+                    tile_body(std::true_type{});
                 TC_TRACE(66 + 8 * i);
             }
             tc_fence_before();
@@ -716,35 +766,55 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
             tc_fence_after();
             const int seq = q_lo + row / G, hq = head * G + row % G;
             const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
-            // O goes out through shared memory: each thread writes its row to the (now
-            // idle) K/V ring with a 16-byte pad per row (the 32 rows of a warp land in
-            // distinct banks), then one bulk copy per row moves it to the workspace
-            constexpr uint32_t OROW = D * 4 + 16;
-            const uint32_t orow = TC_OFF_K + (uint32_t)(my_rt * 128 + my_row) * OROW;
+            // a prefill query group with one unit (one partial): O / l, rounded to T,
+            // straight to out, 16 bytes per store
+            if (PREFILL && out != nullptr && ws.nparts[q_lo] == 1) {
+                const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+                T* dst = out + (int64_t)seq * out_stride + (int64_t)hq * D;
 #pragma unroll
-            for (int cb = 0; cb < D / 32; ++cb) {
-                float ov[32];
-                tmem_ld32(o_col + cb * 32, ov);
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    float ov[32];
+                    tmem_ld32(o_col + cb * 32, ov);
+                    uint32_t pk[16];
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    *reinterpret_cast<float4*>(smem + orow + cb * 128 + k * 16) =
-                        make_float4(ov[4 * k], ov[4 * k + 1], ov[4 * k + 2], ov[4 * k + 3]);
-            }
-            if (row < R) {
-                fence_proxy_async();  // the row's generic writes before the bulk copy reads them
-                bulk_store(ws.part_o + pi * D, sbase + orow, D * 4);
-                ws.part_ml[pi * 2] = m_ref;
-                ws.part_ml[pi * 2 + 1] = l_sum;
-                bulk_wait_read();     // the ring is free again before the next unit streams into it
-            }
-            // A later unit's partial tile leaves the V rows of its missing blocks as they
-            // were, and P V multiplies them by zero probabilities: they must hold finite
-            // values, which fp32 O bits read as bf16 need not be.  Rows staged over the V
-            // ring are cleared (K rows of missing blocks are masked before the softmax).
-            if (orow + OROW > (uint32_t)TC_OFF_V) {
+                    for (int e = 0; e < 16; ++e) pk[e] = Pair<T>::pack(ov[2 * e] * inv, ov[2 * e + 1] * inv);
+                    if (row < R)
 #pragma unroll
-                for (int k = 0; k < (int)OROW / 16; ++k)
-                    *reinterpret_cast<uint4*>(smem + orow + k * 16) = make_uint4(0, 0, 0, 0);
+                        for (int k = 0; k < 4; ++k)
+                            reinterpret_cast<uint4*>(dst + cb * 32)[k] =
+                                make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+                }
+            } else {
+                // O goes out through shared memory: each thread writes its row to the (now
+                // idle) K/V ring with a 16-byte pad per row (the 32 rows of a warp land in
+                // distinct banks), then one bulk copy per row moves it to the workspace
+                constexpr uint32_t OROW = D * 4 + 16;
+                const uint32_t orow = TC_OFF_K + (uint32_t)(my_rt * 128 + my_row) * OROW;
+#pragma unroll
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    float ov[32];
+                    tmem_ld32(o_col + cb * 32, ov);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        *reinterpret_cast<float4*>(smem + orow + cb * 128 + k * 16) =
+                            make_float4(ov[4 * k], ov[4 * k + 1], ov[4 * k + 2], ov[4 * k + 3]);
+                }
+                if (row < R) {
+                    fence_proxy_async();  // the row's generic writes before the bulk copy reads them
+                    bulk_store(ws.part_o + pi * D, sbase + orow, D * 4);
+                    ws.part_ml[pi * 2] = m_ref;
+                    ws.part_ml[pi * 2 + 1] = l_sum;
+                    bulk_wait_read();     // the ring is free again before the next unit streams into it
+                }
+                // A later unit's partial tile leaves the V rows of its missing blocks as they
+                // were, and P V multiplies them by zero probabilities: they must hold finite
+                // values, which fp32 O bits read as bf16 need not be.  Rows staged over the V
+                // ring are cleared (K rows of missing blocks are masked before the softmax).
+                if (orow + OROW > (uint32_t)TC_OFF_V) {
+#pragma unroll
+                    for (int k = 0; k < (int)OROW / 16; ++k)
+                        *reinterpret_cast<uint4*>(smem + orow + k * 16) = make_uint4(0, 0, 0, 0);
+                }
             }
         } else if (leader) {
             // the unit's last P V must be complete before the next unit's first MMA overwrites O

@@ -175,7 +175,7 @@ def paged_prefill(descp, layer: int, slot: torch.Tensor, pos0: int, q: torch.Ten
     stream = torch.cuda.current_stream(q.device).cuda_stream
     for a in range(0, n, PREFILL_QUERIES_PER_LAUNCH):
         m = min(n - a, PREFILL_QUERIES_PER_LAUNCH)
-        parts = int(lib.mentat_prefill_max_parts(m, pos0 + a))
+        parts = int(lib.mentat_prefill_max_parts(descp, m, pos0 + a, hq))
         wsb = int(lib.mentat_decode_workspace_bytes(m, hq, d, parts))
         ws = torch.empty(wsb, device=q.device, dtype=torch.uint8)
         _lib.check(lib.mentat_paged_prefill(
@@ -185,4 +185,4 @@ def paged_prefill(descp, layer: int, slot: torch.Tensor, pos0: int, q: torch.Ten
     return out
 
 
-PREFILL_QUERIES_PER_LAUNCH = 2048
+PREFILL_QUERIES_PER_LAUNCH = 8192

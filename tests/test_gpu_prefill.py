@@ -62,20 +62,26 @@ def _sdpa_fp32(q, k, v, pos0):
     n, hq, d = q.shape
     L, hkv, _ = k.shape
     g = hq // hkv
-    qq = q.float().permute(1, 0, 2)
-    kk = k.float().repeat_interleave(g, dim=1).permute(1, 0, 2)
-    vv = v.float().repeat_interleave(g, dim=1).permute(1, 0, 2)
-    s = torch.matmul(qq, kk.transpose(1, 2)) / d ** 0.5
     mask = torch.arange(L, device=q.device)[None, :] <= (pos0 + torch.arange(n, device=q.device))[:, None]
-    s = s.masked_fill(~mask, float("-inf"))
-    return torch.matmul(torch.softmax(s, dim=-1), vv).permute(1, 0, 2)
+    out = torch.empty((n, hq, d), device=q.device)
+    for h0 in range(0, hq, 8):  # eight query heads at a time bound the score matrix
+        qq = q[:, h0:h0 + 8].float().permute(1, 0, 2)
+        kv = [h // g for h in range(h0, min(hq, h0 + 8))]
+        kk = k[:, kv].float().permute(1, 0, 2)
+        vv = v[:, kv].float().permute(1, 0, 2)
+        s = torch.matmul(qq, kk.transpose(1, 2)) / d ** 0.5
+        s = s.masked_fill(~mask, float("-inf"))
+        out[:, h0:h0 + 8] = torch.matmul(torch.softmax(s, dim=-1), vv).permute(1, 0, 2)
+    return out
 
 
 @pytest.mark.parametrize("dtype,hq,hkv,d,chunks", [
     ("bf16", 32, 4, 128, (700, 1400)),      # crosses the tensor-core kernel's 2,048-token chunk
     ("f16", 16, 16, 64, (5, 1, 300)),
     ("bf16", 8, 1, 128, (2049,)),
-    ("f32", 8, 2, 128, (100, 157, 1)),       # FFMA kernel, 256-token chunks
+    ("f32", 8, 2, 128, (100, 157, 1)),       # FFMA kernel
+    ("bf16", 32, 32, 128, (4096,)),          # every query group in one unit: rows written by the unit kernel
+    ("f16", 64, 8, 64, (3000,)),             # no query with two partials: no merge
 ])
 def test_paged_prefill_in_chunks(dtype, hq, hkv, d, chunks):
     """A prompt appended and attended chunk by chunk (pos0 > 0 for every chunk
