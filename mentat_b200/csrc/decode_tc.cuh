@@ -238,6 +238,40 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 128 consecutive fp32 columns of this thread's TMEM lane (one load, one wait)
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float* v) {
+    uint32_t r[128];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,"
+        "%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
+        "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,"
+        "%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
+        "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+          "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+          "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+          "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+          "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+          "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+          "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+          "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+          "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
@@ -648,27 +682,22 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                 // tile runs the copy without the per-score checks
                 auto tile_body = [&](auto masked_c) {
                     constexpr bool MASKED = decltype(masked_c)::value;
-                    auto ok = [&](int j) {
-                        if constexpr (MASKED) return valid(j);
-                        else return true;
-                    };
-                    // tokens 64-127 stay in registers; tokens 0-63 are read for the max
-                    // here and again, 32 at a time, for their probabilities
-                    float hi[64];
-                    float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
-                    {
-                        float lo[64];
-                        tmem_ld64(s_col, lo);
+                    // the tile's 128 scores in registers: one TMEM load and one wait; a
+                    // masked score becomes -inf, whose probability 2^-inf is 0
+                    float sv[TC_TILE];
+                    tmem_ld128(s_col, sv);
+                    if constexpr (MASKED) {
 #pragma unroll
-                        for (int j = 0; j < 64; ++j) mxs[j & 3] = fmaxf(mxs[j & 3], ok(j) ? lo[j] : -INFINITY);
+                        for (int j = 0; j < TC_TILE; ++j)
+                            if (!valid(j)) sv[j] = -INFINITY;
                     }
-                    tmem_ld64(s_col + 64, hi);
+                    float mxs[8];  // eight independent chains
 #pragma unroll
-                    for (int j = 0; j < 64; ++j) {
-                        if (!ok(64 + j)) hi[j] = -INFINITY;
-                        mxs[j & 3] = fmaxf(mxs[j & 3], hi[j]);
-                    }
-                    const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+                    for (int k = 0; k < 8; ++k) mxs[k] = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < TC_TILE; ++j) mxs[j & 7] = fmaxf(mxs[j & 7], sv[j]);
+                    const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                                           fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
                     float fac = 1.f;
                     const float m_new = fmaxf(m_ref, mx * scale_log2);
                     if (m_ref == -INFINITY || m_new > m_ref + 8.f) {
@@ -693,44 +722,28 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                             tmem_st32(o_col + cb * 32, ov);
                         }
                     }
-                    // P (pairs packed in one column) over the consumed S columns: the P of
-                    // tokens 0-63 lands in columns 0-31, that of tokens 64-127 in 32-63,
-                    // each written after the S columns it overwrites have been read
-                    float accs[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
-                    // SP: also P_lo (prefill, first tile of the sequence only)
+                    // P (pairs packed in one column: token t in column t / 2) over the S
+                    // columns already in registers
+                    float accs[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) accs[k] = 0.f;
+                    // SP: also P_lo, in columns 64 + t / 2 (prefill, first tile of the sequence)
                     auto write_p = [&](auto sp_c) {
                         constexpr bool SP = decltype(sp_c)::value;
 #pragma unroll
-                        for (int cchunk = 0; cchunk < 2; ++cchunk) {
-                            float v[32];
-                            tmem_ld32(s_col + 32 * cchunk, v);
+                        for (int c = 0; c < TC_TILE / 32; ++c) {
                             uint32_t pk[16], pl[SP ? 16 : 1];
 #pragma unroll
                             for (int e = 0; e < 16; ++e) {
-                                const int j = 32 * cchunk + 2 * e;
-                                // a masked score enters as -inf: 2^-inf = 0, no branch
-                                const float a = ex2_approx(fmaf(ok(j) ? v[2 * e] : -INFINITY, scale_log2, neg_m));
-                                const float b = ex2_approx(fmaf(ok(j + 1) ? v[2 * e + 1] : -INFINITY, scale_log2, neg_m));
-                                accs[e & 3] += a + b;
+                                const int j = 32 * c + 2 * e;
+                                const float a = ex2_approx(fmaf(sv[j], scale_log2, neg_m));
+                                const float b = ex2_approx(fmaf(sv[j + 1], scale_log2, neg_m));
+                                accs[e & 7] += a + b;
                                 pk[e] = Pair<T>::pack(a, b);
                                 if constexpr (SP) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
                             }
-                            tmem_st16(s_col + 16 * cchunk, pk);
-                            if constexpr (SP) tmem_st16(s_col + 64 + 16 * cchunk, pl);  // S columns already in hi[]
-                        }
-#pragma unroll
-                        for (int cchunk = 0; cchunk < 2; ++cchunk) {
-                            uint32_t pk[16], pl[SP ? 16 : 1];
-#pragma unroll
-                            for (int e = 0; e < 16; ++e) {
-                                const float a = ex2_approx(fmaf(hi[32 * cchunk + 2 * e], scale_log2, neg_m));
-                                const float b = ex2_approx(fmaf(hi[32 * cchunk + 2 * e + 1], scale_log2, neg_m));
-                                accs[e & 3] += a + b;
-                                pk[e] = Pair<T>::pack(a, b);
-                                if constexpr (SP) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
-                            }
-                            tmem_st16(s_col + 32 + 16 * cchunk, pk);
-                            if constexpr (SP) tmem_st16(s_col + 96 + 16 * cchunk, pl);
+                            tmem_st16(s_col + 16 * c, pk);
+                            if constexpr (SP) tmem_st16(s_col + 64 + 16 * c, pl);
                         }
                     };
                     if constexpr (PSPLIT) {
@@ -742,7 +755,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                         write_p(std::false_type{});
                     }
                     tmem_st_wait();
-                    l_sum += (accs[0] + accs[1]) + (accs[2] + accs[3]);
+                    l_sum += ((accs[0] + accs[1]) + (accs[2] + accs[3])) + ((accs[4] + accs[5]) + (accs[6] + accs[7]));
                 };
                 if (__all_sync(0xffffffffu, full))
                     tile_body(std::false_type{});
