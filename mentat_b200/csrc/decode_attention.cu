@@ -1255,6 +1255,8 @@ extern "C" int mentat_plan_trace_dump(long long* host) {
 extern "C" int mentat_timeline_reset() {
     unsigned long long init[32];
     for (int k = 0; k < 32; ++k) init[k] = (k % 2 == 0) ? ~0ull : 0ull;  // even: first (min), odd: last (max)
+    static long long zero[4096] = {};
+    if (cudaMemcpyToSymbol(mentat::g_tc_trace, zero, sizeof(zero)) != cudaSuccess) return -2;
     return cudaMemcpyToSymbol(mentat::g_timeline, init, sizeof(init)) == cudaSuccess ? 0 : -2;
 }
 extern "C" int mentat_timeline_dump(unsigned long long* host) {

@@ -39,7 +39,9 @@ namespace mentat {
 
 #ifdef MENTAT_TC_TRACE
 __device__ long long g_tc_trace[4096];
-#define TC_TRACE(k) do { if (blockIdx.x == 0 && (threadIdx.x == TC_SOFTMAX_WARPS * 32 || threadIdx.x == 0) && g_trace_on && (k) < 2048) g_tc_trace[(k) + (threadIdx.x ? 0 : 2048)] = clock64(); } while (0)
+// debug builds only: lane 0 of every warp of the CTA that runs work item 0 stamps its events
+// (globaltimer ns) at g_tc_trace[warp * 400 + k]
+#define TC_TRACE(k) do { if ((threadIdx.x & 31) == 0 && g_trace_on && (k) < 400) g_tc_trace[(threadIdx.x >> 5) * 400 + (k)] = (long long)mentat::gtime(); } while (0)
 #else
 #define TC_TRACE(k) do { } while (0)
 #endif
@@ -470,7 +472,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     if (tid == 0 && !wait_probe(smem_u32(&s_probe_bar))) s_abort = 1;  // seen after the loop's first barrier
     TL_FIRST(4);
 #ifdef MENTAT_TC_TRACE
-    bool g_trace_on = true;
+    bool g_trace_on = false;  // the unit of work item 0
 #endif
     // Barrier phases: the K/V rings count tiles (g0); row tile 0 counts every
     // tile and unit, row tile 1 only those of units with two row tiles.
@@ -483,6 +485,9 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
         __syncthreads();
         const int w = s_work;
         if (w >= nwork || s_abort) break;
+#ifdef MENTAT_TC_TRACE
+        g_trace_on = w == 0;
+#endif
         TC_TRACE(0);
         const int u = w / Hkv, head = w % Hkv;
         const int32_t* U = ws.units_tc + (int64_t)u * UNIT_INTS;
