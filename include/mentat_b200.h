@@ -289,6 +289,23 @@ int mentat_gate_step(const void* logits, int32_t dtype, int32_t n, int32_t vocab
                      const double* ema_old, const mentat_gate_params* params,
                      mentat_gate_out* out, cudaStream_t s);
 
+/*
+ * Semantic diversity pruning, pair resolution.  Replaces the masking, the
+ * nonzero().tolist() and the host loop of MentatGenerator._prune_similar
+ * (generator.py:446-484); the similarity matrix itself is the caller's
+ * F.normalize + torch.mm (:441-444).  The leaves of ngroups trees are laid out
+ * tree after tree: tree g owns rows/columns group_off[g] .. group_off[g+1]-1 of
+ * sim ([m][m] of dtype, row stride sim_stride elements; entries between trees
+ * are not read), each tree at most max_group <= 4096 leaves.  parent_key: equal
+ * for siblings (the same parent), distinct otherwise; logp: each leaf's
+ * cumulative log-prob (double); threshold: the similarity threshold rounded to
+ * dtype (torch compares the product in the matrix's dtype).  prune_out: one byte
+ * per leaf, 1 for the leaves the reference's loop prunes.
+ */
+int mentat_prune_similar(const void* sim, int32_t dtype, int64_t sim_stride, const int32_t* group_off,
+                         int32_t ngroups, int32_t max_group, const int64_t* parent_key, const double* logp,
+                         float threshold, uint8_t* prune_out, cudaStream_t s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -83,6 +83,7 @@ SIGNATURES = [
     ("mentat_profile_collect", C.c_int, [C.POINTER(C.c_double), C.POINTER(_I32)]),
     ("mentat_kernel_launch_count", C.c_int64, []),
     ("mentat_gate_step", C.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, C.POINTER(GateParams), _P, _P]),
+    ("mentat_prune_similar", C.c_int, [_P, _I32, _I64, _P, _I32, _I32, _P, _P, _F, _P, _P]),
 ]
 
 _lib = None

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libmentat_b200.so"
-SOURCES = ["kv_cache.cu", "decode_attention.cu", "gate.cu"]
+SOURCES = ["kv_cache.cu", "decode_attention.cu", "gate.cu", "prune.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

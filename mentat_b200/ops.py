@@ -186,3 +186,25 @@ def paged_prefill(descp, layer: int, slot: torch.Tensor, pos0: int, q: torch.Ten
 
 
 PREFILL_QUERIES_PER_LAUNCH = 8192
+
+
+def prune_similar(sim: torch.Tensor, group_off: torch.Tensor, parent_key: torch.Tensor, logp: torch.Tensor,
+                  threshold: float, max_group: int) -> torch.Tensor:
+    """Pair resolution of semantic pruning (``generator.py:446-484``) on the device:
+    ``sim`` (m, m) holds the cosine similarities of the leaves of several trees laid
+    out tree after tree (``group_off`` int32, the trees' first rows and m);
+    ``parent_key`` (int64) is equal for siblings; ``logp`` (float64) the leaves'
+    cumulative log-probs.  Returns one uint8 per leaf, 1 for the pruned ones.
+    Wraps ``mentat_prune_similar``; the threshold is rounded to ``sim``'s dtype,
+    as torch's ``(sim * mask) > threshold`` compares in that dtype."""
+    lib = _lib.load()
+    m = sim.shape[0]
+    out = torch.empty(m, dtype=torch.uint8, device=sim.device)
+    if sim.stride(1) != 1:
+        sim = sim.contiguous()
+    thr = float(torch.tensor(threshold, dtype=sim.dtype).item())
+    stream = torch.cuda.current_stream(sim.device).cuda_stream
+    _lib.check(lib.mentat_prune_similar(sim.data_ptr(), _DT[sim.dtype], sim.stride(0), group_off.data_ptr(),
+                                        group_off.numel() - 1, max_group, parent_key.data_ptr(), logp.data_ptr(),
+                                        thr, out.data_ptr(), stream), "mentat_prune_similar")
+    return out

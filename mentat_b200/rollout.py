@@ -509,9 +509,11 @@ class TreeRollout:
                 node.seq_id = None
 
     def _prune_similar(self, trees, step: int) -> None:                       # :400-497
-        """Semantic pruning of every tree of the step with one similarity matrix
-        and one host read: pairs are compared only inside a tree, never between
-        siblings, and each tree resolves its pairs in (i, j) order."""
+        """Semantic pruning of every tree of the step: one normalize + mm over the
+        warmed-up leaves of all trees, then ``mentat_prune_similar`` masks each
+        tree's pairs (upper triangle, no siblings, none across trees) and resolves
+        them in the reference's row-major order on the device; the host reads one
+        flag per leaf and prunes in the reference's leaf order."""
         groups = []
         for tree in trees:
             cand = [lf for lf in tree.active_leaves()
@@ -521,32 +523,23 @@ class TreeRollout:
         if not groups:
             return
         flat = [lf for _, cand in groups for lf in cand]
-        m = len(flat)
         v = F.normalize(self.sem.rows([lf.sem_row for lf in flat]), p=2, dim=1)
         sim = v @ v.t()
-        key = torch.tensor([[g, id(lf.parent) if lf.parent is not None else -1 - i]
-                            for g, (_, cand) in enumerate(groups) for i, lf in enumerate(cand)],
-                           dtype=torch.int64).to(sim.device, non_blocking=True)
-        mask = torch.triu(torch.ones(m, m, device=sim.device, dtype=torch.bool), diagonal=1)
-        mask &= key[:, :1] == key[:, :1].t()   # same tree
-        mask &= key[:, 1:] != key[:, 1:].t()   # siblings (same parent) are not compared
-        pairs = ((sim * mask) > self.sim_threshold).nonzero(as_tuple=False).tolist()
-        base, gone = [], []
-        off = 0
-        for _, cand in groups:
-            base.append(off)
-            gone.append(set())
-            off += len(cand)
-        owner = [g for g, (_, cand) in enumerate(groups) for _ in cand]
-        for i, j in pairs:
-            g = owner[i]
-            a, b = flat[i], flat[j]
-            if a.node_id in gone[g] or b.node_id in gone[g]:
-                continue
-            gone[g].add(b.node_id if a.cumulative_log_prob >= b.cumulative_log_prob else a.node_id)
+        off = np.zeros(len(groups) + 1, np.int64)
+        np.cumsum([len(cand) for _, cand in groups], out=off[1:])
+        # one host buffer: group offsets, parent keys, cumulative log-probs (8 bytes each)
+        host = np.empty(len(off) + 2 * len(flat), np.int64)
+        host[: len(off)] = off
+        host[len(off): len(off) + len(flat)] = [id(lf.parent) if lf.parent is not None else -1 - i
+                                                for i, lf in enumerate(flat)]
+        host[len(off) + len(flat):].view(np.float64)[:] = [lf.cumulative_log_prob for lf in flat]
+        dev = torch.from_numpy(host).to(sim.device, non_blocking=True)
+        flags = ops.prune_similar(sim, dev[: len(off)].to(torch.int32), dev[len(off): len(off) + len(flat)],
+                                  dev[len(off) + len(flat):].view(torch.float64), self.sim_threshold,
+                                  max(len(cand) for _, cand in groups)).cpu().numpy()
         for g, (tree, cand) in enumerate(groups):
-            for lf in cand:
-                if lf.node_id in gone[g] and lf.is_active:
+            for k, lf in enumerate(cand):
+                if flags[off[g] + k] and lf.is_active:
                     tree.prune(lf)
 
     # ---- rollout -------------------------------------------------------------

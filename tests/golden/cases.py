@@ -127,6 +127,19 @@ PREFILL_CASES = {
 }
 
 
+# semantic pruning (generator.py:400-497): leaves, similarity dtype, cluster spread
+# (smaller: more pairs above the threshold), threshold, min_steps_before_prune
+PRUNE_CASES = {
+    f"p{k}": dict(seed=100 + k, m=m, dtype=dt, spread=sp, thr=thr, min_age=age)
+    for k, (m, dt, sp, thr, age) in enumerate([
+        (2, "f32", 0.1, 0.85, 0), (5, "f32", 0.3, 0.85, 3), (12, "bf16", 0.3, 0.85, 3),
+        (20, "f32", 0.5, 0.85, 5), (33, "bf16", 0.2, 0.85, 2), (40, "f32", 0.4, 0.9, 4),
+        (9, "f32", 1.0, 0.0, 0), (17, "bf16", 0.6, -0.25, 1), (6, "f32", 0.05, 0.85, 9),
+        (37, "bf16", 0.35, 0.8, 3), (24, "f32", 0.25, 0.95, 0), (3, "bf16", 2.0, 0.85, 0),
+    ])
+}
+
+
 def prefill_inputs(name):
     """q (B, S, Hq, D), k and v (B, S, Hkv, D), float32, rounded to the case's dtype."""
     dt, B, S, hq, hkv, d, seed = PREFILL_CASES[name]

@@ -164,6 +164,61 @@ def make_prefill():
     print("prefill cases", len(PREFILL_CASES))
 
 
+def make_prune():
+    """The reference's MentatGenerator._prune_similar on small fake trees: random
+    semantic vectors in clusters (so that pairs cross the threshold), parents
+    shared by sibling groups or None, log-prob ties, leaves too young to compare,
+    and thresholds 0.85 / 0.0 / -0.25.  Stored per case: the similarity matrix the
+    reference computes (same torch ops, same process) over the warmed-up leaves,
+    their parent keys and log-probs, the threshold rounded to the matrix dtype,
+    and the node ids the reference pruned, in its order."""
+    from tests.golden.cases import PRUNE_CASES
+    out = {}
+    for name, c in PRUNE_CASES.items():
+        rng = np.random.default_rng(c["seed"])
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16}[c["dtype"]]
+        m, d = c["m"], 64
+        centers = rng.standard_normal((max(1, m // 3), d))
+        vecs = centers[rng.integers(0, len(centers), m)] + c["spread"] * rng.standard_normal((m, d))
+        pkeys = rng.integers(-1, max(1, m // 4), m)
+        pobj = {int(p): SimpleNamespace(pid=int(p)) for p in set(pkeys.tolist()) if p >= 0}
+        parents = [pobj[int(p)] if p >= 0 else None for p in pkeys]
+        logp = np.round(rng.standard_normal(m) * 3, 1)  # rounded: ties happen
+        ages = rng.integers(0, 8, m)
+        step = 20
+        leaves = [SimpleNamespace(node_id=100 + i, parent=parents[i], creation_step=step - int(ages[i]),
+                                  semantic_vector=torch.from_numpy(vecs[i]).to(dt), cumulative_log_prob=float(logp[i]),
+                                  is_active=True) for i in range(m)]
+        pruned = []
+
+        class Tree:
+            def get_active_leaves(self):
+                return [lf for lf in leaves if lf.is_active]
+
+            def prune_branch(self, lf):
+                lf.is_active = False
+                pruned.append(lf.node_id)
+
+        gen = SimpleNamespace(min_steps_before_prune=c["min_age"], semantic_similarity_threshold=c["thr"],
+                              diversity_pruning_events=[])
+        warm = [lf for lf in leaves if step - lf.creation_step >= c["min_age"]]
+        sv = torch.stack([lf.semantic_vector for lf in warm]) if warm else torch.zeros((0, d), dtype=dt)
+        sim = torch.mm(F.normalize(sv, p=2, dim=1), F.normalize(sv, p=2, dim=1).t()) if len(warm) else sv[:, :0]
+        MentatGenerator._prune_similar(gen, Tree(), step)
+        out[name] = {
+            "sim": sim.float().numpy().tolist(),
+            "parent": [lf.parent.pid if lf.parent is not None else None for lf in warm],
+            "logp": [lf.cumulative_log_prob for lf in warm],
+            "node_id": [lf.node_id for lf in warm],
+            "thr": float(torch.tensor(c["thr"], dtype=dt).item()),
+            "dtype": c["dtype"],
+            "pruned": pruned,
+        }
+    with open(HERE / "prune.json", "w") as f:
+        json.dump(out, f)
+    print("prune cases", len(PRUNE_CASES))
+
+
 def make_gate():
     torch.set_num_threads(1)
     gen_self = SimpleNamespace(soft_explore_window=None, soft_explore_initial=None)
@@ -274,6 +329,6 @@ def make_rollout():
 
 
 if __name__ == "__main__":
-    parts = sys.argv[1:] or ["alloc", "attention", "prefill", "gate", "rollout", "gate_sweep"]
+    parts = sys.argv[1:] or ["alloc", "attention", "prefill", "prune", "gate", "rollout", "gate_sweep"]
     for part in parts:
         globals()[f"make_{part}" if part != "alloc" else "make_alloc_streams"]()

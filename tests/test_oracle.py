@@ -176,3 +176,17 @@ def test_oracle_prefill(name):
     S = q.shape[1]
     for pos0 in sorted({0, S // 3, S - 1}):
         np.testing.assert_array_equal(prefill(q[0][pos0:], k[0], v[0], pos0=pos0), o[0][pos0:])
+
+
+def test_oracle_prune_matches_reference():
+    """The pair-resolution restatement against the reference's _prune_similar on
+    the same similarity matrices (tests/golden/prune.json)."""
+    from oracle.prune import prune_pairs
+    with open(os.path.join(HERE, "golden", "prune.json")) as f:
+        g = json.load(f)
+    assert len(g) >= 10
+    for name, c in g.items():
+        sim = np.asarray(c["sim"], np.float32).reshape(len(c["node_id"]), len(c["node_id"]))
+        gone = prune_pairs(sim, c["parent"], c["logp"], c["thr"])
+        # the reference prunes in its leaf order
+        assert [c["node_id"][i] for i in sorted(gone)] == c["pruned"], name
