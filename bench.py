@@ -51,16 +51,17 @@ def combine_ranks(ms, e2e_ms, kv_bytes, e2e_bytes, device, world):
 
     Every rank decodes its own tree, so the job moves the sum of the ranks'
     bytes in the time of the slowest rank (max over ranks of its device time).
-    Returns (value, e2e value, slowest device time in ms)."""
+    Returns (value, e2e value, slowest device time in ms, [(ms, bytes)] per rank)."""
     import torch.distributed as dist
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=device)
-    tot = torch.tensor([float(kv_bytes), float(e2e_bytes)], dtype=torch.float64, device=device)
+    mine = torch.tensor([ms, e2e_ms, float(kv_bytes), float(e2e_bytes)], dtype=torch.float64, device=device)
+    rows = [mine.clone() for _ in range(world)]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-    ms_max, e2e_max = t.tolist()
-    kv_all, e2e_all = tot.tolist()
-    return kv_all / (ms_max / 1e3) / 1e9, e2e_all / (e2e_max / 1e3) / 1e9, ms_max
+        dist.all_gather(rows, mine)
+    rows = [r.tolist() for r in rows]
+    ms_max, e2e_max = max(r[0] for r in rows), max(r[1] for r in rows)
+    kv_all, e2e_all = sum(r[2] for r in rows), sum(r[3] for r in rows)
+    return (kv_all / (ms_max / 1e3) / 1e9, e2e_all / (e2e_max / 1e3) / 1e9, ms_max,
+            [(r[0], r[2]) for r in rows])
 
 
 def suffixes(seed):
@@ -154,9 +155,11 @@ def build_shape(prefix, suf, seed, device, extra_blocks):
     return m, kids, q
 
 
-def build_tree(seed, device, extra_blocks):
+def build_tree(seed, device, extra_blocks, value_seed=None):
+    """Config 4's tree: suffix lengths drawn from `seed`, K/V and q values from
+    `value_seed` (default `seed`)."""
     suf = suffixes(seed)
-    m, kids, q = build_shape(PREFIX, suf, seed, device, extra_blocks)
+    m, kids, q = build_shape(PREFIX, suf, seed if value_seed is None else value_seed, device, extra_blocks)
     return m, kids, q, suf
 
 
@@ -671,8 +674,11 @@ def run_mentat(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
     lib = _lib.load()
-    m, kids, q, suf = build_tree(args.seed + rank, device,
-                                 extra_blocks=NBR * ((args.steps + args.warmup) // BS + 2))
+    # weak scaling: every rank decodes a tree of the same shape (suffix lengths from the
+    # base seed) with its own values, so the ranks' work is equal and the max over ranks
+    # measures contention, not a larger tree
+    m, kids, q, suf = build_tree(args.seed, device, extra_blocks=NBR * ((args.steps + args.warmup) // BS + 2),
+                                 value_seed=args.seed + rank)
     ub = unique_bytes(PREFIX, suf)
     # host inputs and outputs of the end-to-end loop, made before anything is timed
     # (each step's [q | new K | new V] in one pinned row, so one copy takes them up)
@@ -790,7 +796,7 @@ def run_mentat(args):
     e2e_ms = a0.elapsed_time(a1)
     m.check()
 
-    value, e2e_val, ms_max = combine_ranks(ms, e2e_ms, ub * args.steps, e2e_bytes, device, world)
+    value, e2e_val, ms_max, rank_rows = combine_ranks(ms, e2e_ms, ub * args.steps, e2e_bytes, device, world)
     n_prof = max(cnt.value, 1)
     st_ms = {"plan": stage[0] / n_prof, "units_ffma": stage[1] / n_prof, "units_tc": stage[2] / n_prof,
              "units_tcn": stage[3] / n_prof, "merge": stage[4] / n_prof}
@@ -840,7 +846,13 @@ def run_mentat(args):
                          "traffic": ncu_traffic().get(f"{dom}_c4_bytes_per_launch"),
                          "stage_ms_per_launch": st_ms, "per_kernel": kernels,
                          "whole_call": {"bytes": ub, "ms": ms_max / args.steps,
-                                        "GBps": round(ub / (ms_max / args.steps / 1e3) / 1e9, 1)}},
+                                        "GBps": round(ub / (ms_max / args.steps / 1e3) / 1e9, 1)},
+                         # each rank's own whole-call rate: imbalance shows as spread, contention
+                         # as every rank below the single-GPU figure
+                         "per_rank": [{"rank": r, "ms_per_step": round(t / args.steps, 5),
+                                       "GBps": round(b / (t / 1e3) / 1e9, 1),
+                                       "frac_whole_call": round(b / (t / 1e3) / 1e9 / peak, 4)}
+                                      for r, (t, b) in enumerate(rank_rows)]},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d_bytes,

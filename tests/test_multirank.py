@@ -3,8 +3,9 @@
 Under torchrun every rank decodes its own tree (weak scaling, no data-path
 collective); the job's GB/s is the sum of the ranks' bytes over the slowest
 rank's device time.  Two spawned ranks run ``bench.combine_ranks`` with
-different times and byte counts and must agree on that result.  Each rank's tree
-comes from seed + rank, so the ranks' suffix lengths differ.
+different times and byte counts and must agree on that result, and on each
+rank's own time and bytes.  Every rank's tree has the same shape (suffix lengths
+from the base seed) and its own K/V values (seed + rank).
 """
 
 import os
@@ -56,13 +57,17 @@ def test_two_ranks_sum_bytes_over_slowest_time():
         assert p.exitcode == 0
     want = (4e9 / (12.5 / 1e3) / 1e9, 1.2e9 / (20.0 / 1e3) / 1e9, 12.5)
     for r in range(2):
-        np.testing.assert_allclose(res[r], want, rtol=1e-12)
+        np.testing.assert_allclose(res[r][:3], want, rtol=1e-12)
+        assert res[r][3] == [(10.0, 1e9), (12.5, 3e9)]
 
 
-def test_ranks_decode_different_trees():
+def test_ranks_decode_trees_of_one_shape():
     import sys
     sys.path.insert(0, ROOT)
     import bench
-    a, b = bench.suffixes(4 + 0), bench.suffixes(4 + 1)
-    assert len(a) == len(b) == bench.NBR and not np.array_equal(a, b)
-    assert a.min() >= bench.SUF_LO and a.max() <= bench.SUF_HI
+    # the suffix lengths come from the base seed on every rank (the values from seed + rank)
+    a = bench.suffixes(4)
+    assert len(a) == bench.NBR and a.min() >= bench.SUF_LO and a.max() <= bench.SUF_HI
+    assert not np.array_equal(a, bench.suffixes(5))
+    src = open(os.path.join(ROOT, "bench.py")).read()
+    assert "build_tree(args.seed, device," in src and "value_seed=args.seed + rank" in src
