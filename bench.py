@@ -729,6 +729,24 @@ def run_mentat(args):
     lib.mentat_profile_enable(0)
     m.check()
 
+    # the same decode with the plan a previous call left in the workspace, as every
+    # layer after the first of a decode step runs it (the layers share the tree's
+    # shape; mentat_paged_decode_reuse_plan): reported beside the headline, which
+    # plans every call
+    from mentat_b200 import ops
+    scale = ops.default_scale(D)
+    ops.paged_decode(q, k.slots, max(k.lens), m._op_id, 0, scale)
+    for _ in range(args.warmup):
+        ops.paged_decode(q, k.slots, max(k.lens), m._op_id, 0, scale, reuse_plan=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        ops.paged_decode(q, k.slots, max(k.lens), m._op_id, 0, scale, reuse_plan=True)
+    e1.record()
+    torch.cuda.synchronize()
+    reuse_ms = e0.elapsed_time(e1) / args.steps
+    m.check()
+
     # end to end through the public API: pinned host inputs in, result out, every
     # step.  The copies run on a second stream: step i+1's inputs go up (into the
     # other of two device slots) while step i decodes, and step i's output comes
@@ -847,6 +865,8 @@ def run_mentat(args):
                          "stage_ms_per_launch": st_ms, "per_kernel": kernels,
                          "whole_call": {"bytes": ub, "ms": ms_max / args.steps,
                                         "GBps": round(ub / (ms_max / args.steps / 1e3) / 1e9, 1)},
+                         "whole_call_plan_reused": {"ms": round(reuse_ms, 5),
+                                                    "GBps": round(ub / (reuse_ms / 1e3) / 1e9, 1)},
                          # each rank's own whole-call rate: imbalance shows as spread, contention
                          # as every rank below the single-GPU figure
                          "per_rank": [{"rank": r, "ms_per_step": round(t / args.steps, 5),
