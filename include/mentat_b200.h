@@ -179,8 +179,8 @@ int mentat_paged_decode_reuse_plan(const mentat_kv_cache* c, int32_t layer, cons
  * tokens fit one unit; 0 for invalid arguments).
  * bf16 / fp16 caches with block_size 16 run on the tensor cores (out 16-byte
  * aligned with out_stride a multiple of 8: single-partial rows are written by
- * the unit kernel itself); fp32 on FFMA.  A plan that outgrows max_parts zeroes
- * the output and records MENTAT_DEV_PLAN_OVERFLOW.  Sliding windows are not
+ * the unit kernel itself); fp32 on FFMA.  A max_parts below what the plan needs
+ * returns MENTAT_ERR_ARG and launches nothing.  Sliding windows are not
  * supported.
  */
 int32_t mentat_prefill_max_parts(const mentat_kv_cache* c, int32_t n, int32_t pos0, int32_t num_q_heads);

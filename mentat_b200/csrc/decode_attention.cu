@@ -776,6 +776,9 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
     const float2* po =
         reinterpret_cast<const float2*>(ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + part * 64) + lane;
     const int64_t ostride = (int64_t)Hq * D / 2;  // in float2
+    // prefill: the unit kernel wrote the output of a query with one partial itself; its
+    // part count is read before any partial row (the decode merge loads the rows first)
+    if (skip_single && ws.hdr[HDR_TC_ABORT] == 0 && ws.hdr[HDR_ERR] == 0 && ws.nparts[i] == 1) return;
     // rows up to max_parts exist in the workspace; those past the count get weight 0
     float2 v[B];
 #pragma unroll
@@ -787,8 +790,6 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
     // is clamped so that no row past the workspace is read.
     const bool aborted = ws.hdr[HDR_TC_ABORT] != 0 || ws.hdr[HDR_ERR] != 0;
     const int P = aborted ? 0 : min(ws.nparts[i], max_parts);
-    // prefill: the unit kernel wrote the output of a query with one partial itself
-    if (skip_single && P == 1) return;
     if (ws.hdr[HDR_TC_ABORT] != 0 && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
     // (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
     auto comb = [](float& m, float& l, float m2, float l2) {
@@ -1039,6 +1040,9 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
     const bool pdl = pdl_enabled();
     const int kind = tc_ok ? KIND_TC : KIND_FFMA;
     const int chunk = prefill_chunk_for(n, pos0, G, c->num_kv_heads, kind);
+    // the plan's largest part count is known here: a workspace sized for fewer is refused
+    // before anything runs (the plan kernel's overflow check stays as a guard)
+    if (((int64_t)pos0 + n + chunk - 1) / chunk > max_parts) return MENTAT_ERR_ARG;
     // the tensor-core kernel writes the rows of single-partial queries itself
     const bool direct = tc_ok && (uintptr_t)out % 16 == 0 && out_stride % 8 == 0;
     if (launch(pdl, k_prefill_plan, dim3(1), dim3(1024), 0, s, *c, n, pos0, G, kind, chunk, ws, max_parts) !=
@@ -1062,6 +1066,9 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
             MENTAT_CHECK_LAUNCH();
         }
     }
+    // every query in one unit and written by the tensor-core kernel: nothing to merge
+    // (a unit that gave up a bounded wait records MENTAT_DEV_DECODE_TIMEOUT itself)
+    if (direct && chunk >= pos0 + n) return MENTAT_OK;
     if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
                0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride, direct ? 1 : 0) != cudaSuccess)
         return MENTAT_ERR_CUDA;

@@ -858,7 +858,10 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     bulk_wait_all();
     __syncthreads();
     if (s_abort) {
-        if (leader) atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
+        if (leader) {
+            atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
+            set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);  // also when no merge runs after this kernel
+        }
         if (tma_warp && lane == 0) {
             // at most KST K tiles and VST V tiles can be issued and not yet waited for
             for (uint32_t k = issued > TC_KST ? issued - TC_KST : 0; k < issued; ++k)

@@ -154,3 +154,29 @@ def test_prefill_argument_errors():
         attn_prefill(q, kv, kv, window_size=4)
     assert attn_prefill(q, kv, kv, window_size=8).shape == q.shape  # a window >= S is no window
     assert m.prefill_attention(sid, 0, q[0, :0]).shape == (0, 4, 128)
+
+
+def test_prefill_refuses_a_short_workspace():
+    """A max_parts below the plan's need returns MENTAT_ERR_ARG before any launch."""
+    import ctypes as C
+    from mentat_b200 import _lib
+    lib = _lib.load()
+    m = _manager(torch.float32, 2, 128, blocks=400)
+    sid = m.allocate_sequence()
+    k = torch.randn(5000, 2, 128, device="cuda")
+    m.append_tokens(sid, 0, k, k)
+    q = torch.randn(1, 4, 128, device="cuda")
+    need = int(lib.mentat_prefill_max_parts(m._descp, 1, 4999, 4))
+    assert need > 1
+    ws = torch.empty(int(lib.mentat_decode_workspace_bytes(1, 4, 128, need)), dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(q)
+    slot = m._slots_dev([sid])
+    stream = torch.cuda.current_stream().cuda_stream
+    args = (m._descp, 0, slot.data_ptr(), 1, 4999, q.data_ptr(), 4 * 128, 4, out.data_ptr(), 4 * 128,
+            C.c_float(128 ** -0.5), ws.data_ptr(), ws.numel())
+    assert lib.mentat_paged_prefill(*args, need - 1, stream) == -1
+    assert lib.mentat_paged_prefill(*args, need, stream) == 0
+    torch.cuda.synchronize()
+    m.check()
+    want = _sdpa_fp32(q, k, k, 4999)
+    assert float((out - want).abs().max()) < 1e-5
