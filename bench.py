@@ -181,7 +181,7 @@ TREE_CONFIGS = {
     # the ranks (one KV head per GPU at 8), NCCL all-reduce after o_proj and down_proj
     5: dict(family="qwen3", vocab=151936, hidden=5120, intermediate=25600, layers=64, heads=64, kv_heads=8,
             head_dim=128, rope_theta=1000000.0, prompts=32, prompt_len=4096, max_new_tokens=1024, max_active=32,
-            eos=151645, shard=False, graphs=False, tp=True, tie=False, min_world=4),
+            eos=151645, shard=False, graphs=True, bucket=64, tp=True, tie=False, min_world=4),
 }
 
 
