@@ -75,21 +75,23 @@ def _sdpa_fp32(q, k, v, pos0):
     return out
 
 
-@pytest.mark.parametrize("dtype,hq,hkv,d,chunks", [
-    ("bf16", 32, 4, 128, (700, 1400)),      # crosses the tensor-core kernel's 2,048-token chunk
-    ("f16", 16, 16, 64, (5, 1, 300)),
-    ("bf16", 8, 1, 128, (2049,)),
-    ("f32", 8, 2, 128, (100, 157, 1)),       # FFMA kernel
-    ("bf16", 32, 32, 128, (4096,)),          # every query group in one unit: rows written by the unit kernel
-    ("f16", 64, 8, 64, (3000,)),             # no query with two partials: no merge
+@pytest.mark.parametrize("dtype,hq,hkv,d,chunks,bs", [
+    ("bf16", 32, 4, 128, (700, 1400), 16),  # crosses the tensor-core kernel's 2,048-token chunk
+    ("f16", 16, 16, 64, (5, 1, 300), 16),
+    ("bf16", 8, 1, 128, (2049,), 16),
+    ("f32", 8, 2, 128, (100, 157, 1), 16),   # FFMA kernel
+    ("bf16", 32, 32, 128, (4096,), 16),      # every query group in one unit: rows written by the unit kernel
+    ("f16", 64, 8, 64, (3000,), 16),         # no query with two partials: no merge
+    ("bf16", 32, 2, 128, (1000, 33), 16),    # G = 16: 16 queries per tensor-core unit
+    ("bf16", 8, 2, 128, (300, 90), 32),      # 32-token blocks: the FFMA kernel on bf16
 ])
-def test_paged_prefill_in_chunks(dtype, hq, hkv, d, chunks):
+def test_paged_prefill_in_chunks(dtype, hq, hkv, d, chunks, bs):
     """A prompt appended and attended chunk by chunk (pos0 > 0 for every chunk
     after the first) gives the rows of one causal attention over the prompt."""
     torch.manual_seed(0)
     L = sum(chunks)
     tdt = TORCH_DT[dtype]
-    m = _manager(tdt, hkv, d, blocks=(L + 15) // 16 + 4)
+    m = _manager(tdt, hkv, d, blocks=(L + bs - 1) // bs + 4, bs=bs)
     sid = m.allocate_sequence()
     q = torch.randn(L, hq, d, device="cuda").to(tdt)
     k = torch.randn(L, hkv, d, device="cuda").to(tdt)
