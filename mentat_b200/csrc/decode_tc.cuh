@@ -361,6 +361,29 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
     return (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u + (uint32_t)((chunk ^ (row & 7)) << 4);
 }
 
+// sm_100 packed and three-input forms: one instruction for two FMAs, two adds, or a
+// three-way max (the softmax issues fewer instructions beside the MMA thread)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -700,7 +723,7 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
 #pragma unroll
                     for (int k = 0; k < 8; ++k) mxs[k] = -INFINITY;
 #pragma unroll
-                    for (int j = 0; j < TC_TILE; ++j) mxs[j & 7] = fmaxf(mxs[j & 7], sv[j]);
+                    for (int j = 0; j < TC_TILE; j += 2) mxs[(j >> 1) & 7] = fmax3(mxs[(j >> 1) & 7], sv[j], sv[j + 1]);
                     const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
                                            fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
                     float fac = 1.f;
@@ -729,9 +752,9 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                     }
                     // P (pairs packed in one column: token t in column t / 2) over the S
                     // columns already in registers
-                    float accs[8];
+                    float2 accs[4];  // four independent chains of pair sums
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) accs[k] = 0.f;
+                    for (int k = 0; k < 4; ++k) accs[k] = make_float2(0.f, 0.f);
                     // SP: also P_lo, in columns 64 + t / 2 (prefill, first tile of the sequence)
                     auto write_p = [&](auto sp_c) {
                         constexpr bool SP = decltype(sp_c)::value;
@@ -741,9 +764,11 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
 #pragma unroll
                             for (int e = 0; e < 16; ++e) {
                                 const int j = 32 * c + 2 * e;
-                                const float a = ex2_approx(fmaf(sv[j], scale_log2, neg_m));
-                                const float b = ex2_approx(fmaf(sv[j + 1], scale_log2, neg_m));
-                                accs[e & 7] += a + b;
+                                const float2 x = ffma2(make_float2(sv[j], sv[j + 1]), make_float2(scale_log2, scale_log2),
+                                                       make_float2(neg_m, neg_m));
+                                const float a = ex2_approx(x.x);
+                                const float b = ex2_approx(x.y);
+                                accs[e & 3] = fadd2(accs[e & 3], make_float2(a, b));
                                 pk[e] = Pair<T>::pack(a, b);
                                 if constexpr (SP) pl[e] = Pair<T>::pack(a - Pair<T>::lo(pk[e]), b - Pair<T>::hi(pk[e]));
                             }
@@ -760,7 +785,8 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
                         write_p(std::false_type{});
                     }
                     tmem_st_wait();
-                    l_sum += ((accs[0] + accs[1]) + (accs[2] + accs[3])) + ((accs[4] + accs[5]) + (accs[6] + accs[7]));
+                    l_sum += ((accs[0].x + accs[0].y) + (accs[1].x + accs[1].y)) +
+                             ((accs[2].x + accs[2].y) + (accs[3].x + accs[3].y));
                 };
                 if (__all_sync(0xffffffffu, full))
                     tile_body(std::false_type{});
