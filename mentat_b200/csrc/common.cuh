@@ -82,6 +82,38 @@ static __device__ unsigned long long g_cta_end[2][256];  // per CTA of the wide 
 #endif
 
 // ---------------------------------------------------------------------------
+// sm_100 packed f32x2 arithmetic (one instruction for two IEEE round-to-nearest
+// operations, the same bits as two scalar ones) and the three-input max
+// ---------------------------------------------------------------------------
+#define MENTAT_F32X2_BINARY(name, op)                                                                      \
+    __device__ __forceinline__ float2 name(float2 a, float2 b) {                                          \
+        float2 d;                                                                                         \
+        asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" op \
+            " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                                \
+            : "=f"(d.x), "=f"(d.y)                                                                        \
+            : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                                    \
+        return d;                                                                                         \
+    }
+MENTAT_F32X2_BINARY(fadd2, "add.rn.f32x2")
+MENTAT_F32X2_BINARY(fsub2, "sub.rn.f32x2")
+MENTAT_F32X2_BINARY(fmul2, "mul.rn.f32x2")
+#undef MENTAT_F32X2_BINARY
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+
+// ---------------------------------------------------------------------------
 // element types
 // ---------------------------------------------------------------------------
 template <typename T> struct Elem;

@@ -220,6 +220,53 @@ __device__ __forceinline__ float exp_cw(float d) {
     return __fmul_rn(p, __int_as_float((ki + 127) << 23));                // k >= -126
 }
 
+// exp_cw of two values with packed f32x2 operations: each lane takes exactly the
+// scalar function's operations (IEEE round-to-nearest, no fused multiply-add), so
+// each result has the scalar one's bits
+__device__ __forceinline__ float2 exp_cw2(float2 d) {
+    const float2 kb = fadd2(fmul2(d, f2(0x1.715476p+0f)), f2(12582912.0f));
+    const float2 k = fsub2(kb, f2(12582912.0f));
+    const int kx = __float_as_int(kb.x) - 0x4b400000, ky = __float_as_int(kb.y) - 0x4b400000;
+    const float2 r = fsub2(fsub2(d, fmul2(k, f2(0x1.62e4p-1f))), fmul2(k, f2(0x1.7f7d1cp-20f)));
+    float2 p = f2(0x1.a01a02p-13f);
+    p = fadd2(fmul2(p, r), f2(0x1.6c16c2p-10f));
+    p = fadd2(fmul2(p, r), f2(0x1.111112p-7f));
+    p = fadd2(fmul2(p, r), f2(0x1.555556p-5f));
+    p = fadd2(fmul2(p, r), f2(0x1.555556p-3f));
+    p = fadd2(fmul2(p, r), f2(0.5f));
+    p = fadd2(fmul2(p, r), f2(1.0f));
+    p = fadd2(fmul2(p, r), f2(1.0f));
+    // lanes below -87 (whose k may be out of range) are replaced by 0 below
+    const float2 e = fmul2(p, make_float2(__uint_as_float((uint32_t)(kx + 127) << 23),
+                                          __uint_as_float((uint32_t)(ky + 127) << 23)));
+    return make_float2(d.x >= -87.0f ? e.x : 0.0f, d.y >= -87.0f ? e.y : 0.0f);
+}
+
+// KSum over two chains at once (packed f32x2); value() adds both chains in double
+struct KSum2 {
+    float2 s = make_float2(0.f, 0.f), c = make_float2(0.f, 0.f);
+    __device__ __forceinline__ void add(float2 x) {
+        const float2 y = fsub2(x, c);
+        const float2 t = fadd2(s, y);
+        c = fsub2(fsub2(t, s), y);
+        s = t;
+    }
+    __device__ __forceinline__ double value() const {
+        return ((double)s.x - (double)c.x) + ((double)s.y - (double)c.y);
+    }
+};
+
+// div_rn of two numerators by one divisor (packed f32x2); a lane whose quotient is
+// near the underflow threshold takes the IEEE division, as div_rn does
+__device__ __forceinline__ float2 div_rn2(float2 a, float b, float rb) {
+    const float2 q = fmul2(a, f2(rb));
+    const float2 r = ffma2(make_float2(-q.x, -q.y), f2(b), a);
+    float2 d = ffma2(r, f2(rb), q);
+    if (!(fabsf(q.x) >= 0x1p-124f)) d.x = __fdiv_rn(a.x, b);
+    if (!(fabsf(q.y) >= 0x1p-124f)) d.y = __fdiv_rn(a.y, b);
+    return d;
+}
+
 // Inserts `cur` into the descending list best[0..K); returns the new best[K - 1].
 // Out of line, so that the list lives in local memory and the hot loop keeps
 // only the threshold in registers.
@@ -324,6 +371,26 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
         }
     };
 
+    // g2(i, (xt_i, xt_i+1), (z_i, z_i+1)) for pairs of the cached slice, g1 for single
+    // elements (the slice's tail, or every element when the slice is not cached)
+    auto for_slice2 = [&](auto&& g2, auto&& g1) {
+        if (cache) {
+            const int n = v1 - v0;
+            for (int j = tid * VW; j + VW <= n; j += GATE_THREADS * VW) {
+                const uint4 a = *reinterpret_cast<const uint4*>(xt_s + j);
+                const uint4 b = *reinterpret_cast<const uint4*>(z_s + j);
+#pragma unroll
+                for (int u = 0; u < VW; u += 2)
+                    g2(v0 + j + u, make_float2(vget<T>(a, u), vget<T>(a, u + 1)),
+                       make_float2(vget<T>(b, u), vget<T>(b, u + 1)));
+            }
+            for (int i = n / VW * VW + tid; i < n; i += GATE_THREADS)
+                g1(v0 + i, Elem<T>::to_f(xt_s[i]), Elem<T>::to_f(z_s[i]));
+        } else {
+            from_logits([&](int i, float xt, float z, float) { g1(i, xt, z); });
+        }
+    };
+
     // pass A: maxima of xt and z, the float-accurate entropy's online sums, and
     // the slice copy (16-byte stores when the logits were read 16 bytes at a time)
     float mt = -INFINITY, mz = -INFINITY;
@@ -408,13 +475,20 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
 
     // pass B: S = sum exp(xt - mt) and the penalised one, accumulated in double
     // and rounded to float once: the float sum of the reference, exactly rounded
+    // (pairs in packed f32x2 arithmetic: the same bits per element, half the instructions)
     KSum kt, kz;
-    for_slice([&](int, float xt, float z) {
-        kt.add(exp_cw(__fsub_rn(xt, mt)));
-        kz.add(exp_cw(__fsub_rn(z, mz)));
-    });
-    double St = warp_sum_d(kt.value());
-    double Sz = warp_sum_d(kz.value());
+    KSum2 kt2, kz2;
+    for_slice2(
+        [&](int, float2 xt, float2 z) {
+            kt2.add(exp_cw2(fsub2(xt, f2(mt))));
+            kz2.add(exp_cw2(fsub2(z, f2(mz))));
+        },
+        [&](int, float xt, float z) {
+            kt.add(exp_cw(__fsub_rn(xt, mt)));
+            kz.add(exp_cw(__fsub_rn(z, mz)));
+        });
+    double St = warp_sum_d(kt.value() + kt2.value());
+    double Sz = warp_sum_d(kz.value() + kz2.value());
     if (lane == 0) { s_redd[0][warp] = St; s_redd[1][warp] = Sz; }
     __syncthreads();
     if (warp == 0) {
@@ -448,11 +522,35 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
     // pass C: rounded entropies (terms summed in double) and the top-K of the
     // penalised log-probs
     KSum hs, hz;
+    KSum2 hs2, hz2;
     uint64_t best[MENTAT_GATE_MAXK];
 #pragma unroll
     for (int k = 0; k < MENTAT_GATE_MAXK; ++k) best[k] = 0ull;
     uint64_t kth = 0ull;  // best[K - 1], the smallest key kept
-    for_slice([&](int i, float xt, float z) {
+    // a NaN term counts as 0 (nan_to_num); in the pair form it is added as 0
+    auto term2 = [&](float2 pl) {
+        return make_float2(pl.x == pl.x ? rnd<T>(pl.x) : 0.f, pl.y == pl.y ? rnd<T>(pl.y) : 0.f);
+    };
+    auto pass_c2 = [&](int i, float2 xt, float2 z) {
+        {
+            const float2 dt = fsub2(xt, f2(mt));
+            const float2 q = div_rn2(exp_cw2(dt), Stf, rSt);
+            const float2 l = fsub2(dt, f2(Lt));
+            hs2.add(term2(fmul2(make_float2(rnd<T>(q.x), rnd<T>(q.y)), make_float2(rnd<T>(l.x), rnd<T>(l.y)))));
+        }
+        const float2 dz = fsub2(z, f2(mz));
+        const float2 l = fsub2(dz, f2(Lz));
+        const float lpz0 = rnd<T>(l.x), lpz1 = rnd<T>(l.y);
+        if (want_pen) {
+            const float2 q = div_rn2(exp_cw2(dz), Szf, rSz);
+            hz2.add(term2(fmul2(make_float2(rnd<T>(q.x), rnd<T>(q.y)), make_float2(lpz0, lpz1))));
+        }
+        uint64_t cur = topkey(lpz0, i);
+        if (cur > kth) kth = topk_insert(best, K, cur);  // rare once the list has filled
+        cur = topkey(lpz1, i + 1);
+        if (cur > kth) kth = topk_insert(best, K, cur);
+    };
+    for_slice2(pass_c2, [&](int i, float xt, float z) {
         {
             const float dt = __fsub_rn(xt, mt);
             const float p = rnd<T>(div_rn(exp_cw(dt), Stf, rSt));
@@ -470,8 +568,8 @@ k_gate(const T* __restrict__ logits, int V, int64_t ld, const int32_t* __restric
         const uint64_t cur = topkey(lpz, i);
         if (cur > kth) kth = topk_insert(best, K, cur);  // rare once the list has filled
     });
-    const double Hs = warp_sum_d(hs.value());
-    const double Hz = warp_sum_d(hz.value());
+    const double Hs = warp_sum_d(hs.value() + hs2.value());
+    const double Hz = warp_sum_d(hz.value() + hz2.value());
     if (lane == 0) { s_redd[0][warp] = Hs; s_redd[1][warp] = Hz; }
     warp_topk_merge(K, [&](int head) {
         uint64_t v = 0ull;
