@@ -58,6 +58,9 @@ def attn_decode(q: torch.Tensor, k, v, cu_seqlens_q: torch.Tensor = None, cu_seq
     return out
 
 
+_DENSE_INDEX: dict = {}
+
+
 class _DensePool:
     """A one-layer cache descriptor over the dense (B, S, Hkv, D) K and V of a
     prefill: sequence b is slot b, its blocks are the 16-row slices of k[b]
@@ -79,13 +82,19 @@ class _DensePool:
             p[:, :S] = t
             return p
         self.k, self.v = pool(k), pool(v)
-        i32 = dict(device=dev, dtype=torch.int32)
-        self.tables = torch.arange(B * nb, **i32)
-        self.nblocks = torch.full((B,), nb, **i32)
-        self.ntok = torch.full((B,), S, **i32)
-        self.tail = torch.full((B,), S - (nb - 1) * self.BLOCK, **i32)
-        self.ctrl = torch.zeros(_lib.CTRL_WORDS, device=dev, dtype=torch.int64)
-        self.slots = torch.arange(B, **i32)
+        # the index arrays depend only on (B, S) and the device: made once and reused
+        # by every layer's call (the reference calls attn_prefill once per layer)
+        key = (B, S, dev)
+        idx = _DENSE_INDEX.get(key)
+        if idx is None:
+            i32 = dict(device=dev, dtype=torch.int32)
+            idx = (torch.arange(B * nb, **i32), torch.full((B,), nb, **i32), torch.full((B,), S, **i32),
+                   torch.full((B,), S - (nb - 1) * self.BLOCK, **i32),
+                   torch.zeros(_lib.CTRL_WORDS, device=dev, dtype=torch.int64), torch.arange(B, **i32))
+            if len(_DENSE_INDEX) >= 16:
+                _DENSE_INDEX.clear()
+            _DENSE_INDEX[key] = idx
+        self.tables, self.nblocks, self.ntok, self.tail, self.ctrl, self.slots = idx
         desc = _lib.KVCache()
         desc.num_layers, desc.num_blocks, desc.block_size = 1, B * nb, self.BLOCK
         desc.num_kv_heads, desc.head_dim, desc.dtype = hkv, d, ops._DT[k.dtype]

@@ -566,9 +566,13 @@ k_prefill_plan(mentat_kv_cache c, int n, int pos0, int G, int kind, int chunk, D
                 U[3] = min((ch + 1) * chunk, pos0 + b);
                 U[4] = ch;
             }
-            for (int i = a; i < b; ++i) ws.nparts[i] = min(cnt, max_parts);
         }
         carry += tot;
+    }
+    // every query's part count, one thread per query: its group's chunk count
+    for (int i = tid; i < n; i += blockDim.x) {
+        const int b = min(n, (i / spu + 1) * spu);
+        ws.nparts[i] = min((pos0 + b + chunk - 1) / chunk, max_parts);
     }
     __syncthreads();
     if (tid == 0) {
@@ -998,8 +1002,9 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
 
 // Chunk length of a prefill's units.  A query group's units run one after
 // another on one SM, so a group may take its whole range in one unit (one
-// partial per query, no merge) when that range is no longer than the average
-// work per SM; otherwise its range is cut into chunks of about that average.
+// partial per query, no merge) when that range is at most 1.5 times the average
+// work per SM, or at most 2,048 tokens (16 tiles: shorter than a merge pass
+// costs); otherwise its range is cut into chunks of about that average.
 static int prefill_chunk_for(int n, int pos0, int G, int hkv, int kind) {
     const int64_t L = (int64_t)pos0 + n;
     const int spu = std::max(1, (kind == KIND_TC ? TC_MAX_ROWS : MAX_ROWS) / G);
@@ -1007,7 +1012,7 @@ static int prefill_chunk_for(int n, int pos0, int G, int hkv, int kind) {
     int64_t total = 0;  // tokens seen by all groups: group g's last query is min(n, (g + 1) spu) - 1
     for (int64_t g = 0; g < ngroups; ++g) total += pos0 + std::min<int64_t>(n, (g + 1) * spu);
     const int64_t avg = total * hkv / std::max(1, num_sms());
-    if (L <= avg) return (int)std::min<int64_t>((L + 15) / 16 * 16, INT32_MAX - 15);
+    if (L <= CHUNK_TC || 2 * L <= 3 * avg) return (int)std::min<int64_t>((L + 15) / 16 * 16, INT32_MAX - 15);
     return (int)((std::max<int64_t>(avg, 256) + 127) / 128 * 128);
 }
 
