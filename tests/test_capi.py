@@ -42,3 +42,25 @@ def test_abi_version_and_host_side_sizing():
     # argument errors are reported without touching a device
     assert lib.mentat_kv_init(None, None, None) == -1
     assert lib.mentat_paged_decode(None, 0, None, 0, None, 0, 1, None, 0, 1.0, None, 0, 1, None) == -1
+
+
+def test_prefill_partial_counts():
+    """mentat_prefill_max_parts follows the prefill plan's chunk policy on the host:
+    a range of at most 2,048 tokens, or one within 1.5 times the average work per SM,
+    is one unit (one partial per query); a long range seen by few queries is cut into
+    chunks of about the average work per SM (148 SMs assumed without a device)."""
+    lib = _lib.load()
+    d = _lib.KVCache()
+    d.num_layers, d.num_blocks, d.block_size, d.num_kv_heads, d.head_dim = 1, 1024, 16, 8, 128
+    d.dtype, d.max_seqs, d.max_blocks_per_seq = _lib.MENTAT_BF16, 4, 1024
+    p = ctypes.byref(d)
+    assert lib.mentat_prefill_max_parts(p, 1024, 0, 32) == 1
+    assert lib.mentat_prefill_max_parts(p, 2048, 0, 32) == 1
+    assert lib.mentat_prefill_max_parts(p, 8192, 0, 32) == 1   # 128 query groups fill the GPU
+    # one query after 8,191 cached tokens: 8 units' work spread as 512-token chunks
+    assert lib.mentat_prefill_max_parts(p, 1, 8191, 32) == 16
+    d.dtype = _lib.MENTAT_F32                                   # the FFMA kernel's groups
+    assert lib.mentat_prefill_max_parts(p, 1, 8191, 32) == 16
+    assert lib.mentat_prefill_max_parts(p, 0, 10, 32) == 0      # invalid: no queries
+    assert lib.mentat_prefill_max_parts(p, 4, 0, 30) == 0       # Hq not a multiple of Hkv
+    assert lib.mentat_paged_prefill(None, 0, None, 1, 0, None, 0, 32, None, 0, 1.0, None, 0, 1, None) == -1
