@@ -334,13 +334,15 @@ def tree_measure(cfg_id, seed, rank, world, device):
     return out
 
 
-def _peak_flops():
+def _peak_flops(burst=False):
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
+        if burst:
+            return float(d["bf16_tflops"])
         return float(d.get("bf16_tflops_sustained") or d["bf16_tflops"])
-    return 1400.0
+    return 1590.0 if burst else 1400.0
 
 
 def run_tree(args):
@@ -539,6 +541,43 @@ def run_profile_prefill(args):
             f"{key} {ms * 1e3:.1f} us ({flops / ms / 1e9:.0f} TFLOP/s)" for key, ms in row.items() if key != "S"),
             flush=True)
         del m
+
+
+def prefill_measure(device, seed, steps=10, warmup=3):
+    """Causal prefill attention of one prompt of benchmark configs 3 and 5 (2,048
+    tokens, Llama-3.1-8B heads: Hq 32, Hkv 8; 4,096 tokens, Qwen3-32B heads: Hq 64,
+    Hkv 8; D 128, bf16) through PagedKVCacheManager.prefill_attention, on resident
+    data, CUDA events around `steps` calls; FLOPs count the causal half.  Reported
+    beside the decode headline, not part of it: the rollout's prompt pass."""
+    from mentat_b200 import PagedKVCacheManager
+    g = torch.Generator(device=device).manual_seed(seed)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    peak_burst = _peak_flops(burst=True)
+    out = []
+    for cfg, S, hq, hkv in ((3, 2048, 32, 8), (5, 4096, 64, 8)):
+        d = 128
+        q = torch.randn((S, hq, d), generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn((S, hkv, d), generator=g, device=device).to(torch.bfloat16)
+        m = PagedKVCacheManager(1, hkv, d, max_blocks=(S + 15) // 16 + 2, block_size=16, device=device,
+                                dtype=torch.bfloat16, max_seqs=2)
+        sid = m.allocate_sequence()
+        m.append_tokens(sid, 0, k, k)
+        for _ in range(warmup):
+            m.prefill_attention(sid, 0, q)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            m.prefill_attention(sid, 0, q)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        m.check()
+        tf = 4.0 * hq * d * S * (S + 1) / 2 / (ms / 1e3) / 1e12
+        out.append({"config": cfg, "prompt_tokens": S, "heads": [hq, hkv, d], "us": round(ms * 1e3, 1),
+                    "TFLOPs": round(tf, 1), "frac_of_bf16_burst": round(tf / peak_burst, 4)})
+        del m, q, k
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_profile_case(args):
@@ -840,10 +879,17 @@ def run_mentat(args):
             cpu = cpu_sample(m, kids, q, 2, 12.0)
             cpu.pop("seconds_per_call", None)
     h2d_bytes, d2h_bytes = int(in_host[0].numel() * 2), int(out_host[0].numel() * 2)
-    # tree tokens/s of benchmark config 3 on the same ranks (the prompts split across them)
     del m, k, v, cu, q, in_host
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
+    # causal prefill of the prompts of configs 3 and 5, on rank 0
+    prefill = None
+    if rank == 0 and args.tree:
+        try:
+            prefill = prefill_measure(device, args.seed)
+        except Exception as e:  # noqa: BLE001 - the headline line is printed either way
+            prefill = {"error": f"{type(e).__name__}: {e}"[:300]}
+    # tree tokens/s of benchmark config 3 on the same ranks (the prompts split across them)
     tree = None
     if args.tree:
         try:
@@ -883,6 +929,7 @@ def run_mentat(args):
             "gpu_launches": int(launches),  # counted by the library over the device-timed loop
             "clocks": clk,
             "tree": tree,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
