@@ -42,6 +42,9 @@ constexpr int HDR_NSIMT = 0, HDR_SIMT_NEXT = 1, HDR_ERR = 2, HDR_NTC = 3, HDR_TC
 // the GQA group, and the routing (tensor-core kernels on, narrow kernel on,
 // row threshold)
 constexpr int HDR_PLAN_N = 8, HDR_PLAN_PARTS = 9, HDR_PLAN_G = 10, HDR_PLAN_ROUTE = 11;
+// wide tensor-core CTAs that take units in a decode call (the others leave their
+// SMs to the narrow kernel at once), chosen by the plan
+constexpr int HDR_TC_CTAS = 12;
 constexpr int KIND_FFMA = 0, KIND_TC = 1, KIND_TCN = 2, NKINDS = 3;
 constexpr int UNIT_INTS = 8;        // seq_lo, seq_hi, tok0, tok1, ordinal
 constexpr int CHUNK = 256;          // tokens per FFMA unit
@@ -158,6 +161,8 @@ struct PlanParams {
     int tc_ok;        // dtype / head_dim / block size fit the wide tensor-core kernel
     int narrow_ok;    // ... and the narrow one
     int tc_min_rows;  // rows threshold for the tensor-core kernels
+    int sms;          // SMs of the device
+    int tc_ctas;      // wide tensor-core CTAs that take units (0: the plan chooses)
 };
 
 constexpr int LPT_BUCKETS = CHUNK_TC / 128;  // tensor-core units by 128-token tile count
@@ -176,6 +181,42 @@ __device__ __forceinline__ int seg_chunk(int kind) { return kind == KIND_FFMA ? 
 __device__ __forceinline__ int seg_spu(const PlanParams& pp, int kind) {
     const int rows = kind == KIND_FFMA ? MAX_ROWS : (kind == KIND_TC ? TC_MAX_ROWS : TCN_MAX_ROWS);
     return max(1, rows / pp.G);
+}
+
+// Wide tensor-core CTAs for a decode call, evaluated by one warp.  Wide units
+// are compute bound: about 1.8 us per 128-token tile and 128-row tile on one SM
+// (measured on B200, 256-row units).  Narrow units are memory bound: about 1.4
+// us per 128-token tile on one SM, and at most about 80 tiles (5.2 TB/s) per us
+// over the GPU, less what the wide CTAs fetch meanwhile (wtiles_per_cost tiles
+// per unit of cost).  Both kernels run side by side, the wide one on its CTAs'
+// SMs and the narrow one on the rest, then on all SMs once the wide CTAs are done.
+// Lane k - 1 estimates the end with k wide items per CTA in turn (w = ceil(items
+// / k) CTAs; the wide phase lasts about max(cost / w, longest item)); each extra
+// wave must gain more than 0.2 %.  Wide work alone takes every SM it can use.
+__device__ inline int tc_ctas_warp(int items, float wcost, float wmax, float wtiles_per_cost, float ntiles, int sms,
+                                   int lane) {
+    constexpr float A_W = 1.8f, INV_B_N = 1.f / 1.4f, H_N = 80.f;
+    if (items <= 0) return sms;
+    const int k = lane + 1;
+    const int w = min((items + k - 1) / k, sms);
+    const float tw = A_W * fmaxf(__fdividef(wcost, (float)w), wmax);
+    const float wide_fetch = w * wtiles_per_cost * (1.f / A_W);  // tiles per us the wide CTAs read
+    const float rate = fmaxf(0.f, fminf((sms - w) * INV_B_N, H_N - wide_fetch));
+    const float all_rate = fminf(sms * INV_B_N, H_N);
+    float t = ntiles <= rate * tw ? tw : tw + __fdividef(ntiles - rate * tw, all_rate);
+    t *= 1.f + 0.002f * lane;
+    if (lane >= 8 || (ntiles <= 0.f && lane > 0)) t = 3.0e38f;
+    int bw = w;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float t2 = __shfl_xor_sync(0xffffffffu, t, o);
+        const int w2 = __shfl_xor_sync(0xffffffffu, bw, o);
+        if (t2 < t || (t2 == t && w2 > bw)) {
+            t = t2;
+            bw = w2;
+        }
+    }
+    return max(1, bw);
 }
 
 __global__ void __launch_bounds__(1024)
@@ -204,6 +245,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     __shared__ long long s_scan64[32];
     __shared__ unsigned s_ktot[NKINDS];  // saturating: each term is clamped to FIELD
     __shared__ int s_nnodes, s_err;
+    __shared__ unsigned s_wcost, s_wmax, s_wtiles, s_ntiles;  // work of the tensor-core queues, see tc_ctas_warp
     const int tid = threadIdx.x;
     const int bs = c.block_size;
     // With the LCP kernel ahead of this one (n > 1), the slots and lengths were
@@ -224,6 +266,7 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
         s_h[0] = 0;
         s_h[n] = 0;
         s_err = 0;
+        s_wcost = s_wmax = s_wtiles = s_ntiles = 0;
     }
     __syncthreads();
 
@@ -494,8 +537,29 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
             const int dst = lpt ? atomicAdd(&s_bcnt[bucket_of(rec)], 1) : u;
             int32_t* U = units + (int64_t)dst * UNIT_INTS;
             U[0] = rec[0]; U[1] = rec[1]; U[2] = rec[2]; U[3] = rec[3]; U[4] = rec[4];
+            if (lpt) {  // 128-token tiles of 16-token blocks, as the tensor-core kernels cut them
+                const unsigned nt = (unsigned)(((rec[3] + 15) / 16 - rec[2] / 16 + 7) / 8);
+                const unsigned cw = kind == KIND_TC ? nt * (unsigned)(((rec[1] - rec[0] + 1) * pp.G + 127) / 128) : nt;
+                const unsigned m = __activemask();
+                const unsigned sum = __reduce_add_sync(m, cw), mx = __reduce_max_sync(m, cw);
+                const unsigned tiles = kind == KIND_TC ? __reduce_add_sync(m, nt) : 0u;
+                if ((tid & 31) == __ffs(m) - 1) {
+                    atomicAdd(kind == KIND_TC ? &s_wcost : &s_ntiles, sum);
+                    if (kind == KIND_TC) {
+                        atomicMax(&s_wmax, mx);
+                        atomicAdd(&s_wtiles, tiles);
+                    }
+                }
+            }
         }
         __syncthreads();
+    }
+    if (tid < 32) {
+        const int w = pp.tc_ctas > 0 ? pp.tc_ctas
+                                     : tc_ctas_warp(totals[KIND_TC] * c.num_kv_heads, (float)s_wcost * c.num_kv_heads,
+                                                    (float)s_wmax, (float)s_wtiles / fmaxf(1.f, (float)s_wcost),
+                                                    (float)s_ntiles * c.num_kv_heads, pp.sms, tid);
+        if (tid == 0) ws.hdr[HDR_TC_CTAS] = w;
     }
     __syncthreads();
     PLAN_TRACE(6);
@@ -897,6 +961,19 @@ static bool narrow_enabled() {
     return v != 0;
 }
 
+// wide tensor-core CTAs that take units in a decode call: 0 (default) lets the
+// plan choose from the work of the two tensor-core queues (tc_ctas);
+// MENTAT_TC_CTAS=k fixes it at k
+static int tc_ctas_fixed() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MENTAT_TC_CTAS");
+        v = (e && *e) ? atoi(e) : 0;
+        if (v < 0) v = 0;
+    }
+    return v;
+}
+
 // Decode kernels go out with programmatic stream serialization (pdl_enabled,
 // launch in common.cuh): each may be scheduled while its predecessor on the
 // stream runs, and waits for it with griddep_wait (the narrow kernel waits for
@@ -931,7 +1008,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
             attr[dev] = true;
         }
     }
-    PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows()};
+    PlanParams pp{G, tc_ok ? 1 : 0, narrow_ok ? 1 : 0, tc_min_rows(), num_sms(), tc_ctas_fixed()};
     prof_mark(0, s);
     const bool pdl = pdl_enabled();
     if (reuse_plan) {

@@ -480,8 +480,10 @@ k_units_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ C
     uint32_t issued = 0;  // TMA warp: tiles whose copies have been issued
     const int nunits = ws.hdr[HDR_NTC];
     const int64_t nwork = (int64_t)nunits * Hkv;
+    // a decode call's plan sets how many CTAs take units; the rest leave at once
+    const bool idle = !PREFILL && (int)blockIdx.x >= ws.hdr[HDR_TC_CTAS];
     for (;;) {
-        if (tid == 0) s_work = atomicAdd(&ws.hdr[HDR_TC_NEXT], 1);
+        if (tid == 0) s_work = idle ? INT_MAX : atomicAdd(&ws.hdr[HDR_TC_NEXT], 1);
         __syncthreads();
         const int w = s_work;
         if (w >= nwork || s_abort) break;
