@@ -817,48 +817,69 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// 3. merge: D/64 warps per (sequence, q head), each over 64 output dimensions
-//    (two per lane).  Lane p holds partial p's (m, l); a butterfly of
-//    log-sum-exp combines gives every lane the total (M, L), and lane p's weight
-//    2^(m_p - M) reaches the others by shuffle.  The first 18 partial rows are
-//    all requested before the part count is read; more are taken 18 at a time.
+// 3. merge: one warp per (sequence, q head), lane k over output dimensions
+//    k D/32 .. k D/32 + D/32 - 1.  Lane p holds partial p's (m, l); a butterfly
+//    of log-sum-exp combines gives every lane the total (M, L), and lane p's
+//    weight 2^(m_p - M) reaches the others by shuffle.  The first 18 partial
+//    rows and the first 64 partials' (m, l) are all requested before the part
+//    count is read, so a warp waits for memory once; more rows are taken 18 at
+//    a time.
 // ---------------------------------------------------------------------------
 constexpr int MERGE_WARPS = 4;  // warps per CTA
 
+template <int VL> struct MergeVec;
+template <> struct MergeVec<2> {
+    using type = float2;
+    static __device__ __forceinline__ float at(const float2& v, int k) { return k == 0 ? v.x : v.y; }
+};
+template <> struct MergeVec<4> {
+    using type = float4;
+    static __device__ __forceinline__ float at(const float4& v, int k) {
+        return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+    }
+};
+
 template <typename T, int D>
-__global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
-                                                          int max_parts, T* __restrict__ out, int64_t out_stride,
-                                                          int skip_single) {
-    constexpr int WPP = D / 64;  // warps per (sequence, head)
+__global__ void __launch_bounds__(32 * MERGE_WARPS) k_merge(mentat_kv_cache c, int n, int Hq, DecodeWs ws,
+                                                         int max_parts, T* __restrict__ out, int64_t out_stride,
+                                                         int skip_single) {
+    constexpr int VL = D / 32;   // output elements per lane
     constexpr int B = 18;        // partial rows in flight per lane (config 4 has 17-18 partials)
+    using MV = MergeVec<VL>;
+    using VT = typename MV::type;
     griddep_wait();  // every unit kernel's partials
     griddep_launch();
     TL_FIRST(8);
     const int lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
-    const int pair = gw / WPP, part = gw % WPP;
+    const int pair = blockIdx.x * MERGE_WARPS + (threadIdx.x >> 5);
     if (pair >= n * Hq) return;
     const int i = pair / Hq, hq = pair % Hq;
     const float* ml = ws.part_ml + ((int64_t)i * max_parts * Hq + hq) * 2;  // partial p at ml[p * Hq * 2]
     const int64_t pstride = (int64_t)Hq * 2;
-    const float2* po =
-        reinterpret_cast<const float2*>(ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D + part * 64) + lane;
-    const int64_t ostride = (int64_t)Hq * D / 2;  // in float2
+    const VT* po = reinterpret_cast<const VT*>(ws.part_o + ((int64_t)i * max_parts * Hq + hq) * D) + lane;
+    const int64_t ostride = (int64_t)Hq * D / VL;  // in VT
     // prefill: the unit kernel wrote the output of a query with one partial itself; its
     // part count is read before any partial row (the decode merge loads the rows first)
     if (skip_single && ws.hdr[HDR_TC_ABORT] == 0 && ws.hdr[HDR_ERR] == 0 && ws.nparts[i] == 1) return;
     // rows up to max_parts exist in the workspace; those past the count get weight 0
-    float2 v[B];
+    VT v[B];
 #pragma unroll
     for (int j = 0; j < B; ++j)
         if (j < max_parts) v[j] = po[j * ostride];
+    const float2 ninf = make_float2(-INFINITY, 0.f);
+    const float2 ml_lo = lane < max_parts ? *reinterpret_cast<const float2*>(ml + lane * pstride) : ninf;
+    const float2 ml_hi = lane + 32 < max_parts ? *reinterpret_cast<const float2*>(ml + (lane + 32) * pstride) : ninf;
+    // this lane's (m, l) of partial p = (a multiple of 32) + lane
+    auto ml_of = [&](int p) -> float2 {
+        return p < 32 ? ml_lo : (p < 64 ? ml_hi : *reinterpret_cast<const float2*>(ml + p * pstride));
+    };
     // A failed plan (HDR_ERR) stored part counts that may exceed max_parts and
     // wrote no units; a tensor-core unit kernel that gave up a bounded wait left
     // partials unwritten.  Either way the output is zeroed, and the part count
     // is clamped so that no row past the workspace is read.
     const bool aborted = ws.hdr[HDR_TC_ABORT] != 0 || ws.hdr[HDR_ERR] != 0;
     const int P = aborted ? 0 : min(ws.nparts[i], max_parts);
-    if (ws.hdr[HDR_TC_ABORT] != 0 && gw == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
+    if (ws.hdr[HDR_TC_ABORT] != 0 && pair == 0 && lane == 0) set_error(c, MENTAT_DEV_DECODE_TIMEOUT, 1);
     // (m1, l1) + (m2, l2) = (M, l1 2^(m1 - M) + l2 2^(m2 - M))
     auto comb = [](float& m, float& l, float m2, float l2) {
         const float mn = fmaxf(m, m2);
@@ -869,7 +890,7 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
     for (int p0 = 0; p0 < P; p0 += 32) {
         float m = -INFINITY, l = 0.f;
         if (p0 + lane < P) {
-            const float2 x = *reinterpret_cast<const float2*>(ml + (p0 + lane) * pstride);
+            const float2 x = ml_of(p0 + lane);
             m = x.x;
             l = x.y;
         }
@@ -877,7 +898,9 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
         for (int o = 16; o; o >>= 1) comb(m, l, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, l, o));
         comb(M, L, m, l);
     }
-    float a0 = 0.f, a1 = 0.f;
+    float a[VL];
+#pragma unroll
+    for (int k = 0; k < VL; ++k) a[k] = 0.f;
     for (int b0 = 0; b0 < P; b0 += B) {
         if (b0 > 0) {  // rows after the first batch
 #pragma unroll
@@ -886,22 +909,22 @@ __global__ void __launch_bounds__(32 * MERGE_WARPS, 6) k_merge(mentat_kv_cache c
         }
         // weights of rows b0 .. b0 + B - 1: lane k holds row (b0 & ~31) + k's
         const int w0 = b0 & ~31;
-        const float wlo = w0 + lane < P ? exp2f(ml[(w0 + lane) * pstride] - M) : 0.f;
-        const float whi = w0 + 32 + lane < P ? exp2f(ml[(w0 + 32 + lane) * pstride] - M) : 0.f;
+        const float wlo = w0 + lane < P ? exp2f(ml_of(w0 + lane).x - M) : 0.f;
+        const float whi = w0 + 32 + lane < P ? exp2f(ml_of(w0 + 32 + lane).x - M) : 0.f;
 #pragma unroll
         for (int j = 0; j < B; ++j) {
             const int r = b0 + j - w0;  // < 64: b0 is a multiple of B, w0 = b0 rounded down to 32
             const float wj = __shfl_sync(0xffffffffu, r < 32 ? wlo : whi, r & 31);
             if (b0 + j < P) {
-                a0 = fmaf(v[j].x, wj, a0);
-                a1 = fmaf(v[j].y, wj, a1);
+#pragma unroll
+                for (int k = 0; k < VL; ++k) a[k] = fmaf(MV::at(v[j], k), wj, a[k]);
             }
         }
     }
     const bool ok = P > 0 && L > 0.f && !aborted;
-    T* dst = out + (int64_t)i * out_stride + (int64_t)hq * D + part * 64 + lane * 2;
-    dst[0] = Elem<T>::from_f(ok ? a0 / L : 0.f);
-    dst[1] = Elem<T>::from_f(ok ? a1 / L : 0.f);
+    T* dst = out + (int64_t)i * out_stride + (int64_t)hq * D + lane * VL;
+#pragma unroll
+    for (int k = 0; k < VL; ++k) dst[k] = Elem<T>::from_f(ok ? a[k] / L : 0.f);
     TL_LAST(9);
 }
 
@@ -1068,7 +1091,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
         }
     }
     prof_mark(4, s);
-    if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
+    if (launch(pdl, k_merge<T, D>, dim3((n * Hq + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
                0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride, 0) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
@@ -1151,7 +1174,7 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
     // every query in one unit and written by the tensor-core kernel: nothing to merge
     // (a unit that gave up a bounded wait records MENTAT_DEV_DECODE_TIMEOUT itself)
     if (direct && chunk >= pos0 + n) return MENTAT_OK;
-    if (launch(pdl, k_merge<T, D>, dim3((n * Hq * (D / 64) + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
+    if (launch(pdl, k_merge<T, D>, dim3((n * Hq + MERGE_WARPS - 1) / MERGE_WARPS), dim3(32 * MERGE_WARPS),
                0, s, *c, n, Hq, ws, max_parts, reinterpret_cast<T*>(out), out_stride, direct ? 1 : 0) != cudaSuccess)
         return MENTAT_ERR_CUDA;
     MENTAT_CHECK_LAUNCH();
