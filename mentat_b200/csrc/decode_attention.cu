@@ -984,6 +984,21 @@ static bool narrow_enabled() {
     return v != 0;
 }
 
+// threads of the plan's CTA: at least one per sequence (boundaries and
+// segments are spread over the threads), a multiple of 32, at most 1,024, and
+// at least MENTAT_PLAN_THREADS (default 512: on config 4's 64 sequences the
+// plan takes 1.5 us less than with 1,024 threads, whose block-wide barriers
+// cost more, and 2.3 us less than with 128, which loop over ~900 units)
+static int plan_threads(int n) {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MENTAT_PLAN_THREADS");
+        v = (e && *e) ? atoi(e) : 512;
+        v = std::min(1024, std::max(32, v));
+    }
+    return std::min(1024, (std::max(v, n) + 31) / 32 * 32);
+}
+
 // wide tensor-core CTAs that take units in a decode call: 0 (default) lets the
 // plan choose from the work of the two tensor-core queues (tc_ctas);
 // MENTAT_TC_CTAS=k fixes it at k
@@ -1055,7 +1070,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
                 return MENTAT_ERR_CUDA;
             plan_attr[dev] = true;
         }
-        if (launch(pdl, k_plan, dim3(1), dim3(1024), plan_smem_bytes(n), s, *c, layer, slots, n, pp, ws,
+        if (launch(pdl, k_plan, dim3(1), dim3(plan_threads(n)), plan_smem_bytes(n), s, *c, layer, slots, n, pp, ws,
                    max_parts) != cudaSuccess)
             return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
