@@ -656,7 +656,11 @@ k_prefill_plan(mentat_kv_cache c, int n, int pos0, int G, int kind, int chunk, D
 // 2. units (FFMA path: any dtype, <= 16 query rows per unit)
 // ---------------------------------------------------------------------------
 constexpr int TT = 32;  // tokens per tile
-constexpr int UNIT_THREADS = 128;
+// 16 warps: one query row each in the score stage, and D / 512 of the tile's
+// tokens per thread in the P V stage; a unit's tiles take a quarter of the time
+// they took on 128 threads, which matters when a few long units set the call's
+// time (config 1: 80 work items)
+constexpr int UNIT_THREADS = 512;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(UNIT_THREADS)
@@ -664,12 +668,15 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
         float qscale, DecodeWs ws, int max_parts, int causal_pos0) {
     constexpr int TS = UNIT_THREADS / D;  // token splits in the PV stage
     constexpr int KP = D + 1;             // padded K row (conflict-free column reads)
+    // K and V tiles, and after a unit's last tile the token splits' partial sums
+    constexpr int KV_FLOATS = TT * KP + TT * D, RED_FLOATS = TS * MAX_ROWS * D;
     __shared__ float q_s[MAX_ROWS][D];
-    __shared__ float k_s[TT][KP];
-    __shared__ float v_s[TT][D];
+    __shared__ __align__(16) float kv_red[KV_FLOATS > RED_FLOATS ? KV_FLOATS : RED_FLOATS];
+    float(*k_s)[KP] = reinterpret_cast<float(*)[KP]>(kv_red);
+    float(*v_s)[D] = reinterpret_cast<float(*)[D]>(kv_red + TT * KP);
+    float(*red_s)[MAX_ROWS][D] = reinterpret_cast<float(*)[MAX_ROWS][D]>(kv_red);
     __shared__ float p_s[MAX_ROWS][TT];
     __shared__ float m_s[MAX_ROWS], l_s[MAX_ROWS], a_s[MAX_ROWS];
-    __shared__ float red_s[TS > 1 ? TS : 1][TS > 1 ? MAX_ROWS : 1][TS > 1 ? D : 1];
     __shared__ int s_work;
     griddep_wait();  // the plan
     griddep_launch();
@@ -790,10 +797,10 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
             }
         }
         __syncthreads();
-        if (TS > 1) {
+        if (TS > 1) {  // the tiles' K and V are no longer read: their space takes the partial sums
 #pragma unroll
             for (int r = 0; r < MAX_ROWS; ++r)
-                if (r < R) red_s[TS > 1 ? ts_own : 0][TS > 1 ? r : 0][TS > 1 ? d_own : 0] = acc[r];
+                if (r < R) red_s[ts_own][r][d_own] = acc[r];
             __syncthreads();
         }
         if (ts_own == 0) {
@@ -802,7 +809,7 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
                 if (r < R) {
                     float a = acc[r];
 #pragma unroll
-                    for (int t = 1; t < TS; ++t) a += red_s[t][TS > 1 ? r : 0][TS > 1 ? d_own : 0];
+                    for (int t = 1; t < TS; ++t) a += red_s[t][r][d_own];
                     const int seq = q_lo + r / G, hq = head * G + r % G;
                     const int64_t pi = ((int64_t)seq * max_parts + ord) * Hq + hq;
                     ws.part_o[pi * D + d_own] = a;
@@ -1081,7 +1088,7 @@ static int launch_decode(const mentat_kv_cache* c, int layer, const int32_t* slo
     // a segment has at least G query rows, so with the tensor-core path on and
     // tc_min_rows <= G no unit can land in the FFMA queue
     if (!(tc_ok && tc_min_rows() <= G)) {
-        if (launch(pdl, k_units<T, D>, dim3(num_sms() * 4), dim3(UNIT_THREADS), 0, s, *c, layer, slots, qt, q_stride,
+        if (launch(pdl, k_units<T, D>, dim3(num_sms()), dim3(UNIT_THREADS), 0, s, *c, layer, slots, qt, q_stride,
                    Hq, qscale, ws, max_parts, -1) != cudaSuccess)
             return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
@@ -1172,7 +1179,7 @@ static int launch_prefill(const mentat_kv_cache* c, int layer, const int32_t* sl
     const float qscale = scale * 1.4426950408889634f;  // base-2 softmax
     const T* qt = reinterpret_cast<const T*>(q);
     if (!tc_ok) {
-        if (launch(pdl, k_units<T, D>, dim3(num_sms() * 4), dim3(UNIT_THREADS), 0, s, *c, layer, slot, qt, q_stride,
+        if (launch(pdl, k_units<T, D>, dim3(num_sms()), dim3(UNIT_THREADS), 0, s, *c, layer, slot, qt, q_stride,
                    Hq, qscale, ws, max_parts, pos0) != cudaSuccess)
             return MENTAT_ERR_CUDA;
         MENTAT_CHECK_LAUNCH();
