@@ -712,43 +712,48 @@ k_units(mentat_kv_cache c, int layer, const int32_t* slots, const T* __restrict_
 #pragma unroll
         for (int r = 0; r < MAX_ROWS; ++r) acc[r] = 0.f;
         const int d_own = tid % D, ts_own = tid / D;
-        for (int t0 = t0u; t0 < t1u; t0 += TT) {
+        // K and V rows of a tile: 16-byte loads into registers, all of a thread's in
+        // flight together; the next tile's are requested before this tile's scores
+        constexpr int VEC = 16 / sizeof(T);  // elements per load
+        constexpr int PER = (TT * D / VEC + UNIT_THREADS - 1) / UNIT_THREADS;
+        uint4 kr[PER], vr[PER];
+        auto load_tile = [&](int t0) {
             const int cnt = min(TT, t1u - t0);
-            __syncthreads();
-            {  // K and V rows of the tile: 16-byte loads, all of a thread's in flight together
-                constexpr int VEC = 16 / sizeof(T);                      // elements per load
-                constexpr int PER = (TT * D / VEC + UNIT_THREADS - 1) / UNIT_THREADS;
-                uint4 kr[PER], vr[PER];
 #pragma unroll
-                for (int k = 0; k < PER; ++k) {
-                    const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
-                    if (j < cnt) {
-                        const int p = t0 + j;
-                        const int blk = tab[p / bs];
-                        if ((unsigned)blk < (unsigned)c.num_blocks) {
-                            const int64_t off = pool_row(c, layer, blk, p % bs) + (int64_t)head * D + d;
-                            kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
-                            vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
-                        } else {  // a corrupt table entry: recorded, and read as zeros
-                            set_error(c, MENTAT_DEV_BAD_BLOCK, blk);
-                            kr[k] = vr[k] = make_uint4(0, 0, 0, 0);
-                        }
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < PER; ++k) {
-                    const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
-                    if (j < cnt) {
-                        const T* ke = reinterpret_cast<const T*>(&kr[k]);
-                        const T* ve = reinterpret_cast<const T*>(&vr[k]);
-#pragma unroll
-                        for (int e = 0; e < VEC; ++e) {
-                            k_s[j][d + e] = Elem<T>::to_f(ke[e]);
-                            v_s[j][d + e] = Elem<T>::to_f(ve[e]);
-                        }
+            for (int k = 0; k < PER; ++k) {
+                const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
+                if (j < cnt) {
+                    const int p = t0 + j;
+                    const int blk = tab[p / bs];
+                    if ((unsigned)blk < (unsigned)c.num_blocks) {
+                        const int64_t off = pool_row(c, layer, blk, p % bs) + (int64_t)head * D + d;
+                        kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
+                        vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
+                    } else {  // a corrupt table entry: recorded, and read as zeros
+                        set_error(c, MENTAT_DEV_BAD_BLOCK, blk);
+                        kr[k] = vr[k] = make_uint4(0, 0, 0, 0);
                     }
                 }
             }
+        };
+        if (t0u < t1u) load_tile(t0u);
+        for (int t0 = t0u; t0 < t1u; t0 += TT) {
+            const int cnt = min(TT, t1u - t0);
+            __syncthreads();  // the previous tile's K and V are read
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int idx = tid + k * UNIT_THREADS, j = idx / (D / VEC), d = (idx % (D / VEC)) * VEC;
+                if (j < cnt) {
+                    const T* ke = reinterpret_cast<const T*>(&kr[k]);
+                    const T* ve = reinterpret_cast<const T*>(&vr[k]);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        k_s[j][d + e] = Elem<T>::to_f(ke[e]);
+                        v_s[j][d + e] = Elem<T>::to_f(ve[e]);
+                    }
+                }
+            }
+            if (t0 + TT < t1u) load_tile(t0 + TT);
             __syncthreads();
             {  // scores: lane = token, warps stride the rows
                 const int j = lane;
