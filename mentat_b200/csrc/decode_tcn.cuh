@@ -32,7 +32,7 @@ namespace mentat {
 constexpr int TCN_ROWS = 32;                        // query rows (MMA N)
 constexpr int TCN_TILE = 128;                       // tokens per tile (MMA M)
 constexpr int TCN_NST = 3;                          // K/V stages
-constexpr int TCN_THREADS = 7 * 32;
+constexpr int TCN_THREADS = 8 * 32;  // 4 softmax, MMA, K TMA, scheduler, V TMA
 constexpr int TCN_Q_BYTES = 2 * TCN_ROWS * 128;      // [half][32 rows][128 B]
 constexpr int TCN_KV_STAGE = 2 * TCN_TILE * 128;     // [half][128 tok][128 B] = 32 KB
 constexpr int TCN_P_BYTES = TCN_TILE * TCN_ROWS * 2;  // [128 tok][32 rows] bf16, 64-byte swizzle = 8 KB
@@ -41,7 +41,7 @@ constexpr int TCN_OFF_K = TCN_OFF_Q + 2 * TCN_Q_BYTES;    // two unit slots
 constexpr int TCN_OFF_V = TCN_OFF_K + TCN_NST * TCN_KV_STAGE;
 constexpr int TCN_OFF_P = TCN_OFF_V + TCN_NST * TCN_KV_STAGE;  // two buffers
 constexpr int TCN_OFF_BAR = TCN_OFF_P + 2 * TCN_P_BYTES;
-constexpr int TCN_SMEM = TCN_OFF_BAR + 128 + 1024;
+constexpr int TCN_SMEM = TCN_OFF_BAR + 256 + 1024;
 constexpr uint32_t TCN_TMEM_COLS = 128;             // O^T at 0, S^T[buf] at 32 + 32 * buf
 
 // lane l ends with op over the 32 lanes of a[l]; a[] is clobbered
@@ -98,19 +98,23 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     const bool softmax = warp < 4;
     const bool leader = warp == 4 && lane == 0;
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_full0 = sbase + TCN_OFF_BAR;          // [NST] tile landed
-    const uint32_t bar_s0 = bar_full0 + 8 * TCN_NST;         // [2] S^T buffer written
+    const uint32_t bar_kfull0 = sbase + TCN_OFF_BAR;         // [NST] K tile landed
+    const uint32_t bar_s0 = bar_kfull0 + 8 * TCN_NST;        // [2] S^T buffer written
     const uint32_t bar_pv0 = bar_s0 + 16;                    // [2] P V done, per P buffer
-    const uint32_t bar_empty0 = bar_pv0 + 16;                // [NST] stage consumed
-    const uint32_t bar_ufull0 = bar_empty0 + 8 * TCN_NST;    // [2] unit slot filled (producer)
+    const uint32_t bar_kempty0 = bar_pv0 + 16;               // [NST] K stage read by its Q K^T
+    const uint32_t bar_ufull0 = bar_kempty0 + 8 * TCN_NST;   // [2] unit slot filled (producer)
     const uint32_t bar_uempty0 = bar_ufull0 + 16;            // [2] unit slot released (consumers)
+    const uint32_t bar_vfull0 = bar_uempty0 + 16;            // [NST] V tile landed
+    const uint32_t bar_vempty0 = bar_vfull0 + 8 * TCN_NST;   // [NST] V stage read by its P V
     const int Hkv = c.num_kv_heads, G = Hq / Hkv;
 
     for (int i = tid; i < TCN_OFF_BAR / 16; i += TCN_THREADS) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
         for (int st = 0; st < TCN_NST; ++st) {
-            mbar_init(bar_full0 + 8 * st, 1);
-            mbar_init(bar_empty0 + 8 * st, 1);
+            mbar_init(bar_kfull0 + 8 * st, 1);
+            mbar_init(bar_kempty0 + 8 * st, 1);
+            mbar_init(bar_vfull0 + 8 * st, 1);
+            mbar_init(bar_vempty0 + 8 * st, 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar_s0 + 8 * b, 1);
@@ -141,7 +145,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
 #ifdef MENTAT_TC_TRACE
     bool g_trace_on = true;
 #endif
-    uint32_t issued = 0;  // TMA warp: tiles whose copies have been issued
+    uint32_t issued = 0;  // TMA warps: tiles whose copies have been issued
     const int nunits = ws.hdr[HDR_NTCN];
     const int64_t nwork = (int64_t)nunits * Hkv;
 
@@ -193,10 +197,15 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
             }
             if (!valid) break;
         }
-    } else if (warp == 5) {
-        // TMA warp: streams each published unit's K/V tiles through the stage
-        // ring.  Lanes 0-7 read the tile's block ids (one tile ahead) and each
-        // issues the copies of one block.
+    } else if (warp == 5 || warp == 7) {
+        // TMA warps: warp 5 streams each published unit's K tiles and warp 7 its V
+        // tiles, each through a stage ring of its own (a K stage is free again once
+        // its Q K^T has run, a V stage once its P V has).  Lanes 0-7 read the tile's
+        // block ids (one tile ahead) and each issues the copies of one block.
+        const bool is_k = warp == 5;
+        const CUtensorMap* map = is_k ? &tmap_k : &tmap_v;
+        const uint32_t ring = sbase + (is_k ? TCN_OFF_K : TCN_OFF_V);
+        const uint32_t full0 = is_k ? bar_kfull0 : bar_vfull0, empty0 = is_k ? bar_kempty0 : bar_vempty0;
         for (uint32_t k = 0;; ++k) {
             const int slot = k & 1;
             int ok = 1;
@@ -215,10 +224,10 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                 if (i + 1 < ntiles)
                     next = (lane < 8 && 8 * (i + 1) + lane < nblk) ? checked_block(c, tab[blk0 + 8 * (i + 1) + lane]) : 0;
                 const uint32_t gi = issued, stage = gi % TCN_NST;
-                const uint32_t bar = bar_full0 + 8 * stage;
+                const uint32_t bar = full0 + 8 * stage;
                 if (lane == 0) {
-                    if (gi >= TCN_NST && !mbar_wait(bar_empty0 + 8 * stage, ((gi / TCN_NST) - 1) & 1)) ok = 0;
-                    if (ok) mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2 * 2048));
+                    if (gi >= TCN_NST && !mbar_wait(empty0 + 8 * stage, ((gi / TCN_NST) - 1) & 1)) ok = 0;
+                    if (ok) mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2048));
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) {
@@ -229,8 +238,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
 #pragma unroll
                     for (int h2 = 0; h2 < HALVES; ++h2) {
                         const uint32_t off = stage * TCN_KV_STAGE + h2 * (TCN_TILE * 128) + lane * 2048;
-                        tma_load_3d(sbase + TCN_OFF_K + off, &tmap_k, bar, h2 * 64, head, blk * 16);
-                        tma_load_3d(sbase + TCN_OFF_V + off, &tmap_v, bar, h2 * 64, head, blk * 16);
+                        tma_load_3d(ring + off, map, bar, h2 * 64, head, blk * 16);
                     }
                 }
                 ++issued;
@@ -263,7 +271,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
 
             auto issue_qk = [&](int i) {  // leader: S^T[(g0+i)%2] = K(i) Q^T
                 const uint32_t g = g0 + i, stage = g % TCN_NST;
-                if (!mbar_wait(bar_full0 + 8 * stage, (g / TCN_NST) & 1)) {
+                if (!mbar_wait(bar_kfull0 + 8 * stage, (g / TCN_NST) & 1)) {
                     s_abort = 1;
                     return;
                 }
@@ -275,6 +283,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                              ks > 0);
                 }
                 umma_commit(bar_s0 + 8 * (g & 1));
+                umma_commit(bar_kempty0 + 8 * stage);  // the K stage is free once this Q K^T has run
             };
             if (leader) issue_qk(0);
             // The softmax side only touches the first NR rows (R rounded up to 8).
@@ -386,16 +395,20 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                     TCN_TRACE(14 + 8 * i);
                     if (aborted) break;
                     if (leader) {  // O^T += V(i)^T P(i)^T
-                        tc_fence_after();
                         const uint32_t stage = g % TCN_NST;
-                        for (int ks = 0; ks < TCN_TILE / 16; ++ks) {
-                            const uint32_t va = sbase + TCN_OFF_V + stage * TCN_KV_STAGE + ks * 2048;
-                            const uint32_t pb = sbase + TCN_OFF_P + (g & 1) * TCN_P_BYTES + ks * 1024;
-                            umma_f16(tmem, sdesc_sw128(va, TCN_TILE * 128, 1024), sdesc(pb, TCN_P_BYTES, 512, 4), IDESC_PV,
-                                     (i > 0 || ks > 0));
+                        if (!mbar_wait(bar_vfull0 + 8 * stage, (g / TCN_NST) & 1)) {
+                            s_abort = 1;  // no P V: the softmax warps' next waits give up too
+                        } else {
+                            tc_fence_after();
+                            for (int ks = 0; ks < TCN_TILE / 16; ++ks) {
+                                const uint32_t va = sbase + TCN_OFF_V + stage * TCN_KV_STAGE + ks * 2048;
+                                const uint32_t pb = sbase + TCN_OFF_P + (g & 1) * TCN_P_BYTES + ks * 1024;
+                                umma_f16(tmem, sdesc_sw128(va, TCN_TILE * 128, 1024), sdesc(pb, TCN_P_BYTES, 512, 4),
+                                         IDESC_PV, (i > 0 || ks > 0));
+                            }
+                            umma_commit(bar_pv0 + 8 * (g & 1));
+                            umma_commit(bar_vempty0 + 8 * stage);
                         }
-                        umma_commit(bar_pv0 + 8 * (g & 1));
-                        umma_commit(bar_empty0 + 8 * stage);
                     }
                     TCN_TRACE(15 + 8 * i);
                 }
@@ -460,9 +473,9 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     __syncthreads();
     if (s_abort) {
         if (tid == 0) atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
-        if (warp == 5 && lane == 0)  // every lane counted the same tiles
+        if ((warp == 5 || warp == 7) && lane == 0)  // every lane of a TMA warp counted the same tiles
             for (uint32_t k = issued > TCN_NST ? issued - TCN_NST : 0; k < issued; ++k)
-                (void)mbar_wait(bar_full0 + 8 * (k % TCN_NST), (k / TCN_NST) & 1);
+                (void)mbar_wait((warp == 5 ? bar_kfull0 : bar_vfull0) + 8 * (k % TCN_NST), (k / TCN_NST) & 1);
         __syncthreads();
     }
     tc_fence_before();
