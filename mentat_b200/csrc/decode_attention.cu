@@ -183,40 +183,29 @@ __device__ __forceinline__ int seg_spu(const PlanParams& pp, int kind) {
     return max(1, rows / pp.G);
 }
 
-// Wide tensor-core CTAs for a decode call, evaluated by one warp.  Wide units
-// are compute bound: about 1.8 us per 128-token tile and 128-row tile on one SM
-// (measured on B200, 256-row units).  Narrow units are memory bound: about 1.4
-// us per 128-token tile on one SM, and at most about 80 tiles (5.2 TB/s) per us
-// over the GPU, less what the wide CTAs fetch meanwhile (wtiles_per_cost tiles
-// per unit of cost).  Both kernels run side by side, the wide one on its CTAs'
-// SMs and the narrow one on the rest, then on all SMs once the wide CTAs are done.
-// Lane k - 1 estimates the end with k wide items per CTA in turn (w = ceil(items
-// / k) CTAs; the wide phase lasts about max(cost / w, longest item)); each extra
-// wave must gain more than 0.2 %.  Wide work alone takes every SM it can use.
-__device__ inline int tc_ctas_warp(int items, float wcost, float wmax, float wtiles_per_cost, float ntiles, int sms,
-                                   int lane) {
-    constexpr float A_W = 1.8f, INV_B_N = 1.f / 1.4f, H_N = 80.f;
+// Wide tensor-core CTAs for a decode call, evaluated by one warp.  The wide
+// units are compute bound: about 1.55 us per 128-token tile and 128-row tile
+// on one SM (B200, head_dim 128; in proportion to head_dim).  The narrow units
+// stream at the HBM rate the pair of kernels reaches together, about 5.9 TB/s
+// of K/V tiles on B200.  The call is then shortest when the wide kernel's
+// compute spans the whole stream: lane k - 1 estimates the wide phase with k
+// items per CTA in turn (w = ceil(items / k) CTAs, the phase lasting about
+// max(cost / w, longest item)), and the most waves whose phase still ends
+// within the time both queues' bytes take at that rate win.  When even one
+// wave outlasts the bytes (wide work alone, or little narrow work), every SM
+// the wide items can use takes one.
+__device__ inline int tc_ctas_warp(int items, float wcost, float wmax, float wtiles, float ntiles, int sms,
+                                   int head_dim, int lane) {
     if (items <= 0) return sms;
+    const float a_w = 1.55f * head_dim * (1.f / 128.f);                  // us per tile and row tile
+    const float tiles_per_us = 5.9e6f / (512.f * (float)head_dim);        // 128 tokens x K, V x 2 B
+    const float t_bytes = (wtiles + ntiles) / tiles_per_us;
     const int k = lane + 1;
     const int w = min((items + k - 1) / k, sms);
-    const float tw = A_W * fmaxf(__fdividef(wcost, (float)w), wmax);
-    const float wide_fetch = w * wtiles_per_cost * (1.f / A_W);  // tiles per us the wide CTAs read
-    const float rate = fmaxf(0.f, fminf((sms - w) * INV_B_N, H_N - wide_fetch));
-    const float all_rate = fminf(sms * INV_B_N, H_N);
-    float t = ntiles <= rate * tw ? tw : tw + __fdividef(ntiles - rate * tw, all_rate);
-    t *= 1.f + 0.002f * lane;
-    if (lane >= 8 || (ntiles <= 0.f && lane > 0)) t = 3.0e38f;
-    int bw = w;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float t2 = __shfl_xor_sync(0xffffffffu, t, o);
-        const int w2 = __shfl_xor_sync(0xffffffffu, bw, o);
-        if (t2 < t || (t2 == t && w2 > bw)) {
-            t = t2;
-            bw = w2;
-        }
-    }
-    return max(1, bw);
+    const float tw = a_w * fmaxf(__fdividef(wcost, (float)w), wmax);
+    const unsigned fit = __ballot_sync(0xffffffffu, lane < 8 && tw <= 1.05f * t_bytes);
+    const int best = fit ? __shfl_sync(0xffffffffu, w, 31 - __clz(fit)) : min(items, sms);
+    return max(1, best);
 }
 
 __global__ void __launch_bounds__(1024)
@@ -557,8 +546,8 @@ k_plan(mentat_kv_cache c, int layer, const int32_t* slots, int n, PlanParams pp,
     if (tid < 32) {
         const int w = pp.tc_ctas > 0 ? pp.tc_ctas
                                      : tc_ctas_warp(totals[KIND_TC] * c.num_kv_heads, (float)s_wcost * c.num_kv_heads,
-                                                    (float)s_wmax, (float)s_wtiles / fmaxf(1.f, (float)s_wcost),
-                                                    (float)s_ntiles * c.num_kv_heads, pp.sms, tid);
+                                                    (float)s_wmax, (float)s_wtiles * c.num_kv_heads,
+                                                    (float)s_ntiles * c.num_kv_heads, pp.sms, c.head_dim, tid);
         if (tid == 0) ws.hdr[HDR_TC_CTAS] = w;
     }
     __syncthreads();
