@@ -31,15 +31,23 @@ namespace mentat {
 
 constexpr int TCN_ROWS = 32;                        // query rows (MMA N)
 constexpr int TCN_TILE = 128;                       // tokens per tile (MMA M)
-constexpr int TCN_NST = 3;                          // K/V stages
+#ifndef MENTAT_TCN_KST
+#define MENTAT_TCN_KST 3
+#endif
+#ifndef MENTAT_TCN_VST
+#define MENTAT_TCN_VST 3
+#endif
+constexpr int TCN_KST = MENTAT_TCN_KST;              // K stages (freed after Q K^T)
+constexpr int TCN_VST = MENTAT_TCN_VST;              // V stages (freed after P V)
+static_assert(TCN_KST >= 2 && TCN_VST >= 2 && TCN_KST + TCN_VST <= 6, "six 32 KB stages fit beside Q and P");
 constexpr int TCN_THREADS = 8 * 32;  // 4 softmax, MMA, K TMA, scheduler, V TMA
 constexpr int TCN_Q_BYTES = 2 * TCN_ROWS * 128;      // [half][32 rows][128 B]
 constexpr int TCN_KV_STAGE = 2 * TCN_TILE * 128;     // [half][128 tok][128 B] = 32 KB
 constexpr int TCN_P_BYTES = TCN_TILE * TCN_ROWS * 2;  // [128 tok][32 rows] bf16, 64-byte swizzle = 8 KB
 constexpr int TCN_OFF_Q = 0;
 constexpr int TCN_OFF_K = TCN_OFF_Q + 2 * TCN_Q_BYTES;    // two unit slots
-constexpr int TCN_OFF_V = TCN_OFF_K + TCN_NST * TCN_KV_STAGE;
-constexpr int TCN_OFF_P = TCN_OFF_V + TCN_NST * TCN_KV_STAGE;  // two buffers
+constexpr int TCN_OFF_V = TCN_OFF_K + TCN_KST * TCN_KV_STAGE;
+constexpr int TCN_OFF_P = TCN_OFF_V + TCN_VST * TCN_KV_STAGE;  // two buffers
 constexpr int TCN_OFF_BAR = TCN_OFF_P + 2 * TCN_P_BYTES;
 constexpr int TCN_SMEM = TCN_OFF_BAR + 256 + 1024;
 constexpr uint32_t TCN_TMEM_COLS = 128;             // O^T at 0, S^T[buf] at 32 + 32 * buf
@@ -99,20 +107,22 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     const bool leader = warp == 4 && lane == 0;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_kfull0 = sbase + TCN_OFF_BAR;         // [NST] K tile landed
-    const uint32_t bar_s0 = bar_kfull0 + 8 * TCN_NST;        // [2] S^T buffer written
+    const uint32_t bar_s0 = bar_kfull0 + 8 * TCN_KST;        // [2] S^T buffer written
     const uint32_t bar_pv0 = bar_s0 + 16;                    // [2] P V done, per P buffer
     const uint32_t bar_kempty0 = bar_pv0 + 16;               // [NST] K stage read by its Q K^T
-    const uint32_t bar_ufull0 = bar_kempty0 + 8 * TCN_NST;   // [2] unit slot filled (producer)
+    const uint32_t bar_ufull0 = bar_kempty0 + 8 * TCN_KST;   // [2] unit slot filled (producer)
     const uint32_t bar_uempty0 = bar_ufull0 + 16;            // [2] unit slot released (consumers)
     const uint32_t bar_vfull0 = bar_uempty0 + 16;            // [NST] V tile landed
-    const uint32_t bar_vempty0 = bar_vfull0 + 8 * TCN_NST;   // [NST] V stage read by its P V
+    const uint32_t bar_vempty0 = bar_vfull0 + 8 * TCN_VST;   // [VST] V stage read by its P V
     const int Hkv = c.num_kv_heads, G = Hq / Hkv;
 
     for (int i = tid; i < TCN_OFF_BAR / 16; i += TCN_THREADS) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
-        for (int st = 0; st < TCN_NST; ++st) {
+        for (int st = 0; st < TCN_KST; ++st) {
             mbar_init(bar_kfull0 + 8 * st, 1);
             mbar_init(bar_kempty0 + 8 * st, 1);
+        }
+        for (int st = 0; st < TCN_VST; ++st) {
             mbar_init(bar_vfull0 + 8 * st, 1);
             mbar_init(bar_vempty0 + 8 * st, 1);
         }
@@ -206,6 +216,7 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
         const CUtensorMap* map = is_k ? &tmap_k : &tmap_v;
         const uint32_t ring = sbase + (is_k ? TCN_OFF_K : TCN_OFF_V);
         const uint32_t full0 = is_k ? bar_kfull0 : bar_vfull0, empty0 = is_k ? bar_kempty0 : bar_vempty0;
+        const uint32_t nst = is_k ? TCN_KST : TCN_VST;
         for (uint32_t k = 0;; ++k) {
             const int slot = k & 1;
             int ok = 1;
@@ -223,10 +234,10 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                 const int nb = min(8, nblk - 8 * i);
                 if (i + 1 < ntiles)
                     next = (lane < 8 && 8 * (i + 1) + lane < nblk) ? checked_block(c, tab[blk0 + 8 * (i + 1) + lane]) : 0;
-                const uint32_t gi = issued, stage = gi % TCN_NST;
+                const uint32_t gi = issued, stage = gi % nst;
                 const uint32_t bar = full0 + 8 * stage;
                 if (lane == 0) {
-                    if (gi >= TCN_NST && !mbar_wait(empty0 + 8 * stage, ((gi / TCN_NST) - 1) & 1)) ok = 0;
+                    if (gi >= nst && !mbar_wait(empty0 + 8 * stage, ((gi / nst) - 1) & 1)) ok = 0;
                     if (ok) mbar_expect_tx(bar, (uint32_t)(nb * HALVES * 2048));
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -270,8 +281,8 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
             if (tid < TCN_ROWS) s_mref[tid] = -INFINITY;  // warp 0; read by others only after the vote barriers
 
             auto issue_qk = [&](int i) {  // leader: S^T[(g0+i)%2] = K(i) Q^T
-                const uint32_t g = g0 + i, stage = g % TCN_NST;
-                if (!mbar_wait(bar_kfull0 + 8 * stage, (g / TCN_NST) & 1)) {
+                const uint32_t g = g0 + i, stage = g % TCN_KST;
+                if (!mbar_wait(bar_kfull0 + 8 * stage, (g / TCN_KST) & 1)) {
                     s_abort = 1;
                     return;
                 }
@@ -395,8 +406,8 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
                     TCN_TRACE(14 + 8 * i);
                     if (aborted) break;
                     if (leader) {  // O^T += V(i)^T P(i)^T
-                        const uint32_t stage = g % TCN_NST;
-                        if (!mbar_wait(bar_vfull0 + 8 * stage, (g / TCN_NST) & 1)) {
+                        const uint32_t stage = g % TCN_VST;
+                        if (!mbar_wait(bar_vfull0 + 8 * stage, (g / TCN_VST) & 1)) {
                             s_abort = 1;  // no P V: the softmax warps' next waits give up too
                         } else {
                             tc_fence_after();
@@ -473,9 +484,11 @@ k_units_tcn(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ 
     __syncthreads();
     if (s_abort) {
         if (tid == 0) atomicExch(&ws.hdr[HDR_TC_ABORT], 1);
-        if ((warp == 5 || warp == 7) && lane == 0)  // every lane of a TMA warp counted the same tiles
-            for (uint32_t k = issued > TCN_NST ? issued - TCN_NST : 0; k < issued; ++k)
-                (void)mbar_wait((warp == 5 ? bar_kfull0 : bar_vfull0) + 8 * (k % TCN_NST), (k / TCN_NST) & 1);
+        if ((warp == 5 || warp == 7) && lane == 0) {  // every lane of a TMA warp counted the same tiles
+            const uint32_t nst = warp == 5 ? TCN_KST : TCN_VST;
+            for (uint32_t k = issued > nst ? issued - nst : 0; k < issued; ++k)
+                (void)mbar_wait((warp == 5 ? bar_kfull0 : bar_vfull0) + 8 * (k % nst), (k / nst) & 1);
+        }
         __syncthreads();
     }
     tc_fence_before();
