@@ -13,9 +13,11 @@
 // more than 2^8 (then O^T's column and the running sums are rescaled); the
 // per-row sums stay in registers, one partial per thread, and are reduced once
 // per unit with a 31-shuffle transpose-reduce.
-// Roles: warps 0-3 softmax, warp 4 lane 0 MMA issue, warp 5 TMA issue (lanes
-// 0-7, one 16-token block each), warp 6 claims units and stages their Q rows
-// into one of two unit slots while the current unit runs.
+// Roles: warps 0-3 softmax, warp 4 lane 0 MMA issue, warps 5 and 7 TMA issue
+// of K and of V (lanes 0-7, one 16-token block each), each through a stage ring
+// of its own (a K stage is free once its Q K^T has run, a V stage once its P V
+// has), warp 6 claims units and stages their Q rows into one of two unit slots
+// while the current unit runs.
 // Every mbarrier wait is bounded (TC_WAIT_CYCLES); on timeout the CTA records
 // HDR_TC_ABORT, drains its copies in flight and frees its TMEM.
 
